@@ -1,0 +1,153 @@
+/*
+ * awqb200.h - C ABI of the B200 (sm_100a) AWQ W4A16 quantized-linear library.
+ *
+ * Every entry point is plain C: device pointers, sizes, a dtype code and a
+ * CUDA stream passed as void* (cudaStream_t). Each returns 0 on success or a
+ * non-zero status; awqb_last_error() then holds a message for the calling
+ * thread. No entry point allocates device memory or synchronises the device
+ * unless its comment says so, so the GEMM paths can be captured in CUDA graphs.
+ *
+ * Status codes:
+ *   0 ok, 1 invalid argument, 2 unsupported shape/config, 3 CUDA error,
+ *   4 NCCL error, 5 a bounded device-side wait gave up.
+ *
+ * Each declaration cites the reference (SGLite) interface it replaces, by path
+ * inside python/sglite/.
+ */
+#ifndef AWQB200_H
+#define AWQB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AWQB_ABI_VERSION 1
+
+enum { AWQB_DTYPE_F16 = 0, AWQB_DTYPE_BF16 = 1 };
+
+/* Message describing the last failure on this thread ("" if none).
+ * Replaces host::PanicError messages, kernels/csrc/include/sglite/utils.h:42-92. */
+const char* awqb_last_error(void);
+int awqb_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Weight repack (load time).
+ * Replaces awq_marlin_repack + marlin_permute_scales + awq_to_marlin_zero_points
+ * called from AWQMarlinLinearMethod.process_weights_after_loading,
+ * srt/model_executor/layers/quantization/awq_marlin.py:270-334.
+ *
+ * AWQ inputs (awq.py:87-124): qweight int32 [batch][K][N/8], qzeros int32
+ * [batch][K/G][N/8], scales (fp16 or bf16 bits) [batch][K/G][N]. batch > 1
+ * repacks stacked MoE experts ([E, K, N/8], weight_loader.py:134-142).
+ * G must be 32, 64 or a multiple of 128, K % G == 0, N % 8 == 0.
+ */
+int awqb_blob_bytes(int64_t K, int64_t N, int64_t G, int64_t* bytes);
+int awqb_repack(const int32_t* qweight, const int32_t* qzeros, const uint16_t* scales,
+                int64_t batch, int64_t K, int64_t N, int64_t G, void* blob, void* stream);
+/* Exact inverse of awqb_repack (used to prove the repack is lossless). */
+int awqb_unrepack(const void* blob, int64_t batch, int64_t K, int64_t N, int64_t G,
+                  int32_t* qweight, int32_t* qzeros, uint16_t* scales, void* stream);
+/* W[batch][K][N] = (q - z) * s in the activation dtype, with the GEMM's own
+ * dequantisation routine; bit-exact with the reference unpack + dequantise,
+ * layers/quantization/awq_triton.py:53-62,94-96,119-122. */
+int awqb_dequant(const void* blob, int64_t batch, int64_t K, int64_t N, int64_t G, int dtype,
+                 void* w, void* stream);
+
+/* ------------------------------------------------------------------------
+ * W4A16 GEMM: y[M][N] = x[M][K] * dequant(blob)[K][N] (+ bias[N]).
+ * Replaces awq_gemm_triton, layers/quantization/awq_triton.py:144-195 (called by
+ * AWQLinearMethod.apply_weights, awq.py:126-147) and gptq_marlin_gemm through
+ * apply_awq_marlin_linear, marlin_utils.py:355-415.
+ * x, y, bias are in the activation dtype; x 16-byte aligned, rows contiguous.
+ * fp32 accumulation. The workspace (size from awqb_gemm_workspace_bytes) must
+ * be 256-byte aligned and zero-filled before its first use; every call leaves
+ * it zero-filled again. Calls that share a workspace must not overlap in time.
+ */
+int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t G, int64_t* bytes);
+int awqb_gemm(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+              const void* blob, const void* bias, void* y, void* workspace,
+              int64_t workspace_bytes, void* stream);
+/* Same with an explicit token tile (16, 32, 64, 128, 256; 0 = default) and CTA
+ * count (0 = one per SM); for tuning and tests. */
+int awqb_gemm_workspace_bytes_ex(int64_t M, int64_t K, int64_t N, int64_t G, int ntok,
+                                 int64_t ctas, int64_t* bytes);
+int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                 const void* blob, const void* bias, void* y, void* workspace,
+                 int64_t workspace_bytes, int ntok, int64_t ctas, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MoE (Qwen3-MoE experts). The reference runs dense experts through
+ * FusedMoe.forward, srt/model_executor/layers/fused_moe/fused.py:205-233;
+ * these entry points give the same pipeline over AWQ expert weights.
+ */
+/* softmax over E router logits (fp32) and top-k; renormalize divides by the
+ * top-k sum and then by (sum + 1e-8). Replaces fused_topk, fused.py:11-31. */
+int awqb_moe_topk_softmax(const float* logits, int64_t M, int64_t E, int64_t topk,
+                          int renormalize, float* topk_weights, int32_t* topk_ids, void* stream);
+/* Length of sorted_ids needed by awqb_moe_align. */
+int64_t awqb_moe_max_padded(int64_t numel, int64_t num_experts, int64_t block_m);
+/* Sort the numel = M*topk (token, k) pairs routed to experts [e_begin, e_end)
+ * by expert (stable), pad each expert to block_m with the sentinel numel, write
+ * the local expert index of every block and the padded row count.
+ * Replaces moe_align_block_size, fused.py:34-61. */
+int awqb_moe_align(const int32_t* topk_ids, int64_t numel, int64_t e_begin, int64_t e_end,
+                   int64_t block_m, int32_t* sorted_ids, int64_t max_padded,
+                   int32_t* block_expert, int32_t* num_post_pad, void* stream);
+/* out[r] = x[sorted_ids[r] / topk] (zero for padding rows), r < *num_post_pad.
+ * Stands in for the row gather done by fused_moe_kernel's a_ptrs,
+ * kernels/triton/fused_moe.py:241. */
+int awqb_moe_gather_rows(const void* x, int64_t K, const int32_t* sorted_ids,
+                         const int32_t* num_post_pad, int64_t numel, int64_t topk,
+                         int64_t rows_max, void* out, void* stream);
+/* Grouped W4A16 GEMM over expert-sorted rows: blobs holds one blob per expert,
+ * blob_stride bytes apart (awqb_repack with batch = E). ntok must equal the
+ * align block size. Optional row_map / row_scale scatter rows to
+ * row_map[r] (< num_valid) and multiply by row_scale[that row].
+ * Replaces fused_moe_kernel, kernels/triton/fused_moe.py:155-285. */
+int awqb_moe_grouped_workspace_bytes(int64_t rows_max, int64_t K, int64_t N, int64_t G, int ntok,
+                                     int64_t* bytes);
+int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N, int64_t G,
+                          int dtype, const void* blobs, int64_t blob_stride,
+                          const int32_t* block_expert, const int32_t* num_post_pad, int ntok,
+                          const int32_t* row_map, const float* row_scale, int64_t num_valid,
+                          void* y, int64_t ldy, void* workspace, int64_t workspace_bytes,
+                          void* stream);
+/* out[r][j] = silu(in[r][j]) * in[r][I + j] in fp32; rows = min(rows_max,
+ * *rows_dev) when rows_dev is given. Replaces silu_and_mul (flashinfer),
+ * srt/model_executor/layers/activation.py:11-15. */
+int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
+                      int dtype, void* out, void* stream);
+/* out[m][h] = sum_k in[m][k][h] (fp32 accumulate), counting only pairs whose
+ * expert is in [e_begin, e_end) when topk_ids is given.
+ * Replaces moe_sum_reduce_triton, kernels/moe_triton.py:68-102. */
+int awqb_moe_topk_sum(const void* in, int64_t M, int64_t topk, int64_t H, const int32_t* topk_ids,
+                      int64_t e_begin, int64_t e_end, int dtype, void* out, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor-parallel all-reduce. Replaces NCCLWrapper (create_nccl_uid, ctor,
+ * all_reduce), kernels/csrc/src/pynccl.cu:75-189, used through
+ * PyNCCLDistributedImpl.all_reduce, srt/distributed/communicator.py:62-65.
+ * sym_bytes > 0 allocates an ncclMemAlloc buffer registered as a symmetric
+ * window (the reference's max_bytes buffer); reductions up to that size are
+ * staged through it. awqb_nccl_init allocates (NCCL-owned) memory.
+ */
+int awqb_nccl_unique_id_bytes(void);
+int awqb_nccl_get_unique_id(uint8_t* out);
+int awqb_nccl_init(const uint8_t* uid, int rank, int world, int64_t sym_bytes, void** comm);
+int awqb_nccl_symmetric_buffer(void* comm, void** ptr, int64_t* bytes);
+int awqb_nccl_all_reduce(void* comm, void* buf, int64_t count, int dtype, void* stream);
+int awqb_nccl_destroy(void* comm);
+
+/* Device-side error word (bits set when a bounded wait inside a kernel gave
+ * up). Both calls synchronise the current device. */
+int awqb_device_error(uint32_t* out);
+int awqb_clear_device_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AWQB200_H */

@@ -1,0 +1,325 @@
+// Host side of the W4A16 GEMM: argument checks, tile-size choice, TMA tensor
+// map for the activations, launch, and the C-ABI entry points declared in
+// include/awqb200.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "awqb200.h"
+#include "awqb_common.h"
+#include "awqb_gemm.cuh"
+
+namespace awqb {
+
+__device__ uint32_t g_awqb_err;  // OR of DeviceError bits, cleared by awqb_clear_device_error
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+uint32_t* device_err_ptr() {
+  static uint32_t* ptrs[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_awqb_err) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<uint32_t*>(p);
+  }
+  return ptrs[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Activation tensor map: rows of K 16-bit elements, box = 64 elements x ntok
+// rows, 128-byte swizzle, out-of-range rows/columns read as zero.
+int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, int ntok) {
+  auto enc = tensor_map_encoder();
+  AWQB_REQUIRE(enc != nullptr, kCudaError, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)ntok};
+  cuuint32_t estride[2] = {1u, 1u};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(x), gdim, gstride, box,
+                   estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AWQB_REQUIRE(r == CUDA_SUCCESS, kCudaError, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return kOk;
+}
+
+int choose_ntok(int64_t M) {
+  if (M <= 16) return 16;
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128) return 128;
+  return 256;
+}
+
+struct Plan {
+  int ntok, gpb;
+  int NT, KB, MT;
+  int64_t ctas;
+  int64_t cnt_bytes, part_bytes;
+};
+
+int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
+
+bool valid_group(int64_t G) { return G == 32 || G == 64 || (G >= 128 && G % 128 == 0); }
+
+int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, Plan* pl) {
+  AWQB_REQUIRE(M >= 0 && K > 0 && N > 0, kInvalidArgument, "bad GEMM sizes M=%lld K=%lld N=%lld",
+               (long long)M, (long long)K, (long long)N);
+  AWQB_REQUIRE(valid_group(G), kUnsupported, "group size %lld not supported (32, 64 or a multiple of 128)",
+               (long long)G);
+  AWQB_REQUIRE(K % G == 0, kInvalidArgument, "K=%lld is not a multiple of the group size %lld",
+               (long long)K, (long long)G);
+  AWQB_REQUIRE(N % 8 == 0, kInvalidArgument, "N=%lld is not a multiple of 8", (long long)N);
+  AWQB_REQUIRE(M < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31), kUnsupported, "sizes too large");
+  pl->ntok = ntok > 0 ? ntok : choose_ntok(M);
+  AWQB_REQUIRE(pl->ntok == 16 || pl->ntok == 32 || pl->ntok == 64 || pl->ntok == 128 ||
+                   pl->ntok == 256,
+               kInvalidArgument, "token tile %d not built", pl->ntok);
+  pl->gpb = groups_per_block((int)G);
+  pl->NT = (int)(round_up(N, kBlockN) / kBlockN);
+  pl->KB = (int)(round_up(K, kBlockK) / kBlockK);
+  pl->MT = (int)((M + pl->ntok - 1) / pl->ntok);
+  const int64_t U = (int64_t)pl->MT * pl->NT * pl->KB;
+  int64_t c = ctas > 0 ? ctas : device_sm_count();
+  if (c > U) c = U;
+  if (c < 1) c = 1;
+  pl->ctas = c;
+  pl->cnt_bytes = round_up((int64_t)pl->MT * pl->NT * 4, 256);
+  pl->part_bytes = c * 2 * 128 * (int64_t)pl->ntok * 4;
+  return kOk;
+}
+
+template <typename T, int NTOK, int GPB>
+int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, cudaStream_t stream) {
+  using Cfg = GemmCfg<NTOK, GPB>;
+  auto kern = awq_gemm_kernel<T, NTOK, GPB>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  AWQB_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    AWQB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set[dev] = true;
+  }
+  kern<<<dim3((unsigned)ctas), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream>>>(tm, p);
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+template <typename T, int NTOK>
+int launch_g(const CUtensorMap& tm, const GemmParams& p, int gpb, int64_t ctas, cudaStream_t s) {
+  switch (gpb) {
+    case 1: return launch_t<T, NTOK, 1>(tm, p, ctas, s);
+    case 2: return launch_t<T, NTOK, 2>(tm, p, ctas, s);
+    case 4: return launch_t<T, NTOK, 4>(tm, p, ctas, s);
+  }
+  AWQB_REQUIRE(false, kUnsupported, "groups per block %d not built", gpb);
+  return kUnsupported;
+}
+
+template <typename T>
+int launch_n(const CUtensorMap& tm, const GemmParams& p, const Plan& pl, cudaStream_t s) {
+  switch (pl.ntok) {
+    case 16: return launch_g<T, 16>(tm, p, pl.gpb, pl.ctas, s);
+    case 32: return launch_g<T, 32>(tm, p, pl.gpb, pl.ctas, s);
+    case 64: return launch_g<T, 64>(tm, p, pl.gpb, pl.ctas, s);
+    case 128: return launch_g<T, 128>(tm, p, pl.gpb, pl.ctas, s);
+    case 256: return launch_g<T, 256>(tm, p, pl.gpb, pl.ctas, s);
+  }
+  AWQB_REQUIRE(false, kUnsupported, "token tile %d not built", pl.ntok);
+  return kUnsupported;
+}
+
+int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+              const void* blob, const void* bias, void* y, void* workspace,
+              int64_t workspace_bytes, int ntok, int64_t ctas, void* stream) {
+  AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
+               "dtype %d is not fp16 (0) or bf16 (1)", dtype);
+  Plan pl;
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl);
+  if (st != kOk) return st;
+  if (M == 0) return kOk;
+  AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
+  AWQB_REQUIRE(((uintptr_t)x & 15) == 0, kInvalidArgument, "x must be 16-byte aligned");
+  AWQB_REQUIRE(((uintptr_t)blob & 15) == 0, kInvalidArgument, "blob must be 16-byte aligned");
+  AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
+               "workspace must be non-null and 256-byte aligned");
+  AWQB_REQUIRE(workspace_bytes >= pl.cnt_bytes + pl.part_bytes, kInvalidArgument,
+               "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
+               (long long)(pl.cnt_bytes + pl.part_bytes));
+  uint32_t* err = device_err_ptr();
+  AWQB_REQUIRE(err != nullptr, kCudaError, "cannot resolve the device error word");
+
+  CUtensorMap tm;
+  st = make_x_tensor_map(&tm, x, M, K, pl.ntok);
+  if (st != kOk) return st;
+
+  GemmParams p{};
+  p.blob = static_cast<const uint8_t*>(blob);
+  p.bias = bias;
+  p.y = y;
+  p.ldy = N;
+  p.num_valid = 0;
+  p.M = (int32_t)M;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.NT = pl.NT;
+  p.KB = pl.KB;
+  p.MT = pl.MT;
+  p.ws_cnt = static_cast<int32_t*>(workspace);
+  p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
+  p.err = err;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
+  return launch_n<__nv_bfloat16>(tm, p, pl, s);
+}
+
+}  // namespace
+}  // namespace awqb
+
+using namespace awqb;
+
+extern "C" int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t G,
+                                         int64_t* bytes) {
+  Plan pl;
+  int st = make_plan(M, K, N, G, 0, 0, &pl);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
+  *bytes = pl.cnt_bytes + pl.part_bytes;
+  return kOk;
+}
+
+extern "C" int awqb_gemm_workspace_bytes_ex(int64_t M, int64_t K, int64_t N, int64_t G, int ntok,
+                                            int64_t ctas, int64_t* bytes) {
+  Plan pl;
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
+  *bytes = pl.cnt_bytes + pl.part_bytes;
+  return kOk;
+}
+
+extern "C" int awqb_gemm(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                         const void* blob, const void* bias, void* y, void* workspace,
+                         int64_t workspace_bytes, void* stream) {
+  return gemm_impl(x, M, K, N, G, dtype, blob, bias, y, workspace, workspace_bytes, 0, 0, stream);
+}
+
+extern "C" int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                            const void* blob, const void* bias, void* y, void* workspace,
+                            int64_t workspace_bytes, int ntok, int64_t ctas, void* stream) {
+  return gemm_impl(x, M, K, N, G, dtype, blob, bias, y, workspace, workspace_bytes, ntok, ctas,
+                   stream);
+}
+
+extern "C" int awqb_device_error(uint32_t* out) {
+  AWQB_REQUIRE(out != nullptr, kInvalidArgument, "out is null");
+  AWQB_CUDA(cudaDeviceSynchronize());
+  AWQB_CUDA(cudaMemcpyFromSymbol(out, g_awqb_err, sizeof(uint32_t)));
+  return kOk;
+}
+
+extern "C" int awqb_clear_device_error(void) {
+  const uint32_t zero = 0;
+  AWQB_CUDA(cudaDeviceSynchronize());
+  AWQB_CUDA(cudaMemcpyToSymbol(g_awqb_err, &zero, sizeof(uint32_t)));
+  return kOk;
+}
+
+// ---------------------------------------------------------------------------
+// Grouped GEMM over expert-sorted rows (MoE). Row block b (ntok rows) uses the
+// weights of expert block_expert[b]; only the first *num_post_pad rows are
+// computed (a device value, so the call needs no host sync and can be
+// captured). With row_map, output row = row_map[r] and rows mapping to
+// >= num_valid (padding) are skipped; with row_scale the output row is scaled
+// by row_scale[output row] (the router weight, fused.py:183-196 with
+// MUL_ROUTED_WEIGHT, triton/fused_moe.py:276-278).
+namespace awqb {
+namespace {
+int64_t grouped_ctas(int64_t ctas) { return ctas > 0 ? ctas : device_sm_count(); }
+}  // namespace
+}  // namespace awqb
+
+extern "C" int awqb_moe_grouped_workspace_bytes(int64_t rows_max, int64_t K, int64_t N, int64_t G,
+                                                int ntok, int64_t* bytes) {
+  Plan pl;
+  int st = make_plan(rows_max, K, N, G, ntok, 0, &pl);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
+  const int64_t c = grouped_ctas(0);
+  *bytes = pl.cnt_bytes + c * 2 * 128 * (int64_t)pl.ntok * 4;
+  return kOk;
+}
+
+extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
+                                     int64_t G, int dtype, const void* blobs, int64_t blob_stride,
+                                     const int32_t* block_expert, const int32_t* num_post_pad,
+                                     int ntok, const int32_t* row_map, const float* row_scale,
+                                     int64_t num_valid, void* y, int64_t ldy, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
+               "dtype %d is not fp16 (0) or bf16 (1)", dtype);
+  AWQB_REQUIRE(ntok == 16 || ntok == 32 || ntok == 64 || ntok == 128 || ntok == 256,
+               kInvalidArgument, "block size %d must equal a built token tile", ntok);
+  Plan pl;
+  int st = make_plan(rows_max, K, N, G, ntok, 0, &pl);
+  if (st != kOk) return st;
+  if (rows_max == 0) return kOk;
+  pl.ctas = grouped_ctas(0);
+  pl.part_bytes = pl.ctas * 2 * 128 * (int64_t)pl.ntok * 4;
+  AWQB_REQUIRE(x_sorted && blobs && block_expert && num_post_pad && y, kInvalidArgument, "null pointer");
+  AWQB_REQUIRE(((uintptr_t)x_sorted & 15) == 0 && ((uintptr_t)blobs & 15) == 0 && blob_stride % 16 == 0,
+               kInvalidArgument, "x_sorted, blobs and blob_stride must be 16-byte aligned");
+  AWQB_REQUIRE(ldy >= N, kInvalidArgument, "ldy < N");
+  AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
+               "workspace must be non-null and 256-byte aligned");
+  AWQB_REQUIRE(workspace_bytes >= pl.cnt_bytes + pl.part_bytes, kInvalidArgument,
+               "workspace too small: %lld < %lld bytes", (long long)workspace_bytes,
+               (long long)(pl.cnt_bytes + pl.part_bytes));
+  uint32_t* err = device_err_ptr();
+  AWQB_REQUIRE(err != nullptr, kCudaError, "cannot resolve the device error word");
+  CUtensorMap tm;
+  st = make_x_tensor_map(&tm, x_sorted, rows_max, K, pl.ntok);
+  if (st != kOk) return st;
+  GemmParams p{};
+  p.blob = static_cast<const uint8_t*>(blobs);
+  p.blob_stride = blob_stride;
+  p.tile_expert = block_expert;
+  p.rows_valid = num_post_pad;
+  p.y = y;
+  p.ldy = ldy;
+  p.row_map = row_map;
+  p.row_scale = row_scale;
+  p.num_valid = (int32_t)num_valid;
+  p.M = (int32_t)rows_max;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.NT = pl.NT;
+  p.KB = pl.KB;
+  p.MT = pl.MT;
+  p.ws_cnt = static_cast<int32_t*>(workspace);
+  p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
+  p.err = err;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
+  return launch_n<__nv_bfloat16>(tm, p, pl, s);
+}

@@ -1,0 +1,310 @@
+// MoE routing and glue kernels around the grouped AWQ GEMM.
+//
+// Reference behaviour (layers/fused_moe/fused.py):
+//   fused_topk (:11-31)          softmax over router logits, top-k, optional
+//                                renormalisation (inside topk_softmax), then a
+//                                second division by (sum + 1e-8) (:26-27).
+//   moe_align_block_size (:34-61) (token, k) pairs sorted by expert, each
+//                                expert's list padded to the block size with the
+//                                sentinel M*topk; one expert id per block.
+//   silu_and_mul (activation.py:11-15), moe_sum_reduce (triton/fused_moe.py:7-50).
+// Expert parallelism (experts [e_begin, e_end) on this rank) is new here: pairs
+// routed to other ranks' experts are dropped from the local sort and the sum.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "awqb200.h"
+#include "awqb_common.h"
+
+namespace awqb {
+namespace {
+
+constexpr int kMaxExperts = 512;
+constexpr int kMaxTopk = 32;
+
+// One warp per token. Top-k is chosen on the logits (softmax is monotonic),
+// ties going to the lower expert index, so the choice does not depend on the
+// rounding of exp.
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int M, int E, int topk,
+                                    int renormalize, float* __restrict__ w_out,
+                                    int32_t* __restrict__ id_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= M) return;
+  const float* row = logits + (int64_t)warp * E;
+  float mx = -INFINITY;
+  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+  for (int e = lane; e < E; e += 32) sum += expf(row[e] - mx);
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+
+  uint32_t taken[kMaxExperts / 32] = {};
+  float wsel[kMaxTopk];
+  int isel[kMaxTopk];
+  float wsum = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < E; e += 32) {
+      if (taken[e >> 5] & (1u << (e & 31))) continue;
+      const float v = row[e];
+      if (v > bv || (v == bv && e < bi)) { bv = v; bi = e; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    taken[bi >> 5] |= 1u << (bi & 31);
+    const float p = expf(bv - mx) / sum;
+    wsel[k] = p;
+    isel[k] = bi;
+    wsum += p;
+  }
+  if (lane == 0) {
+    float* wo = w_out + (int64_t)warp * topk;
+    int32_t* io = id_out + (int64_t)warp * topk;
+    if (renormalize) {
+      float s2 = 0.f;
+      for (int k = 0; k < topk; ++k) { wsel[k] = wsel[k] / wsum; s2 += wsel[k]; }
+      for (int k = 0; k < topk; ++k) wsel[k] = wsel[k] / (s2 + 1e-8f);
+    }
+    for (int k = 0; k < topk; ++k) { wo[k] = wsel[k]; io[k] = isel[k]; }
+  }
+}
+
+// Single CTA of 1024 threads (32 warps). Warp w owns the contiguous slice
+// [w*S, (w+1)*S) of the flattened (token, k) ids and emits its pairs in index
+// order, so the sort is stable and deterministic.
+__global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__ ids, int numel, int e_begin,
+                                                     int e_end, int block_m, int max_padded,
+                                                     int32_t* __restrict__ sorted_ids,
+                                                     int32_t* __restrict__ block_expert,
+                                                     int32_t* __restrict__ num_post_pad) {
+  extern __shared__ int32_t sm[];
+  const int E = e_end - e_begin;
+  int32_t* cnt = sm;                    // [32][E] per-warp counts, then per-warp write bases
+  int32_t* off = sm + 32 * E;           // [E + 1] padded offsets
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int slice = (numel + 31) / 32;
+  const int s0 = warp * slice;
+  const int s1 = min(numel, s0 + slice);
+
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) cnt[i] = 0;
+  for (int i = threadIdx.x; i < max_padded; i += blockDim.x) sorted_ids[i] = numel;
+  __syncthreads();
+  for (int i = s0 + lane; i < s1; i += 32) {
+    const int e = ids[i] - e_begin;
+    if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < E; ++e) {
+      off[e] = run;
+      int tot = 0;
+      for (int w = 0; w < 32; ++w) tot += cnt[w * E + e];
+      run += (tot + block_m - 1) / block_m * block_m;
+    }
+    off[E] = run;
+    *num_post_pad = run;
+  }
+  __syncthreads();
+  // per-warp write bases: off[e] + counts of lower warps
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = off[e];
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+  }
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    for (int b = off[e] / block_m; b < off[e + 1] / block_m; ++b) block_expert[b] = e;
+  }
+  __syncthreads();
+  for (int base = s0; base < s1; base += 32) {
+    const int i = base + lane;
+    const bool live = i < s1;
+    int e = live ? ids[i] - e_begin : -1;
+    if (e < 0 || e >= E) e = -1;
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) {
+      const int rank = __popc(grp & ((1u << lane) - 1u));
+      sorted_ids[cnt[warp * E + e] + rank] = i;
+    }
+    __syncwarp();
+    if (e >= 0 && (grp & ((1u << lane) - 1u)) == 0) cnt[warp * E + e] += __popc(grp);
+    __syncwarp();
+  }
+}
+
+// x_sorted[r] = x[sorted_ids[r] / topk] for live rows, zero for padding rows.
+__global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ sorted_ids,
+                                   const int32_t* __restrict__ num_post_pad, int numel, int topk,
+                                   int rows_max, int vec_per_row, uint4* __restrict__ out) {
+  const int rows = min(*num_post_pad, rows_max);
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < (int64_t)rows * vec_per_row;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(t / vec_per_row);
+    const int v = (int)(t - (int64_t)r * vec_per_row);
+    const int sid = sorted_ids[r];
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (sid < numel) val = x[(int64_t)(sid / topk) * vec_per_row + v];
+    out[t] = val;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v) { return (float)v; }
+
+// out[r, j] = silu(in[r, j]) * in[r, I + j], computed in fp32.
+template <typename T>
+__global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
+                                    const int32_t* __restrict__ rows_dev, int I, T* __restrict__ out) {
+  int64_t rows = rows_max;
+  if (rows_dev != nullptr && (int64_t)*rows_dev < rows) rows = *rows_dev;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * I;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / I;
+    const int j = (int)(t - r * I);
+    const float g = to_f(in[r * 2 * I + j]);
+    const float u = to_f(in[r * 2 * I + I + j]);
+    out[t] = (T)(g / (1.0f + expf(-g)) * u);
+  }
+}
+
+// out[m, h] = sum over k of in[m, k, h] (fp32 accumulate). With ids given,
+// only pairs whose expert lies in [e_begin, e_end) are summed.
+template <typename T>
+__global__ void topk_sum_kernel(const T* __restrict__ in, int M, int topk, int H,
+                                const int32_t* __restrict__ ids, int e_begin, int e_end,
+                                T* __restrict__ out) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < (int64_t)M * H;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = t / H;
+    const int h = (int)(t - m * H);
+    float acc = 0.f;
+    for (int k = 0; k < topk; ++k) {
+      if (ids != nullptr) {
+        const int e = ids[m * topk + k];
+        if (e < e_begin || e >= e_end) continue;
+      }
+      acc += to_f(in[(m * topk + k) * H + h]);
+    }
+    out[t] = (T)acc;
+  }
+}
+
+unsigned grid1d(int64_t items, int threads) {
+  int64_t b = (items + threads - 1) / threads;
+  if (b > 148 * 32) b = 148 * 32;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+}  // namespace awqb
+
+using namespace awqb;
+
+extern "C" int awqb_moe_topk_softmax(const float* logits, int64_t M, int64_t E, int64_t topk,
+                                     int renormalize, float* topk_weights, int32_t* topk_ids,
+                                     void* stream) {
+  AWQB_REQUIRE(M >= 0 && E >= 1 && E <= kMaxExperts && topk >= 1 && topk <= kMaxTopk && topk <= E,
+               kInvalidArgument, "bad routing sizes M=%lld E=%lld topk=%lld", (long long)M,
+               (long long)E, (long long)topk);
+  if (M == 0) return kOk;
+  AWQB_REQUIRE(logits && topk_weights && topk_ids, kInvalidArgument, "null pointer");
+  const int threads = 256;
+  const unsigned blocks = (unsigned)((M * 32 + threads - 1) / threads);
+  topk_softmax_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, (int)M, (int)E, (int)topk, renormalize, topk_weights, topk_ids);
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+extern "C" int64_t awqb_moe_max_padded(int64_t numel, int64_t num_experts, int64_t block_m) {
+  return numel + num_experts * (block_m - 1);
+}
+
+extern "C" int awqb_moe_align(const int32_t* topk_ids, int64_t numel, int64_t e_begin, int64_t e_end,
+                              int64_t block_m, int32_t* sorted_ids, int64_t max_padded,
+                              int32_t* block_expert, int32_t* num_post_pad, void* stream) {
+  const int64_t E = e_end - e_begin;
+  AWQB_REQUIRE(E >= 1 && E <= kMaxExperts && e_begin >= 0, kInvalidArgument,
+               "bad expert range [%lld, %lld)", (long long)e_begin, (long long)e_end);
+  AWQB_REQUIRE(block_m >= 1 && numel >= 0 && numel < (1ll << 30), kInvalidArgument, "bad sizes");
+  AWQB_REQUIRE(max_padded >= numel + E * (block_m - 1), kInvalidArgument,
+               "sorted_ids too small: %lld < %lld", (long long)max_padded,
+               (long long)(numel + E * (block_m - 1)));
+  AWQB_REQUIRE(sorted_ids && block_expert && num_post_pad && (numel == 0 || topk_ids),
+               kInvalidArgument, "null pointer");
+  const size_t smem = (size_t)(32 * E + E + 1) * sizeof(int32_t);
+  auto kern = align_kernel;
+  AWQB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, (int)numel, (int)e_begin, (int)e_end, (int)block_m, (int)max_padded, sorted_ids,
+      block_expert, num_post_pad);
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+extern "C" int awqb_moe_gather_rows(const void* x, int64_t K, const int32_t* sorted_ids,
+                                    const int32_t* num_post_pad, int64_t numel, int64_t topk,
+                                    int64_t rows_max, void* out, void* stream) {
+  AWQB_REQUIRE(K % 8 == 0 && K > 0, kInvalidArgument, "K=%lld must be a positive multiple of 8",
+               (long long)K);
+  AWQB_REQUIRE(x && sorted_ids && num_post_pad && out, kInvalidArgument, "null pointer");
+  AWQB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)out & 15) == 0, kInvalidArgument,
+               "x and out must be 16-byte aligned");
+  const int vec = (int)(K / 8);
+  gather_rows_kernel<<<grid1d(rows_max * vec, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(x), sorted_ids, num_post_pad, (int)numel, (int)topk, (int)rows_max,
+      vec, static_cast<uint4*>(out));
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
+                                 int dtype, void* out, void* stream) {
+  AWQB_REQUIRE(I > 0 && rows_max >= 0, kInvalidArgument, "bad sizes");
+  AWQB_REQUIRE(in && out, kInvalidArgument, "null pointer");
+  if (rows_max == 0) return kOk;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned g = grid1d(rows_max * I, 256);
+  if (dtype == AWQB_DTYPE_F16)
+    silu_and_mul_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(in), rows_max, rows_dev,
+                                                   (int)I, static_cast<__half*>(out));
+  else if (dtype == AWQB_DTYPE_BF16)
+    silu_and_mul_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), rows_max,
+                                                          rows_dev, (int)I,
+                                                          static_cast<__nv_bfloat16*>(out));
+  else
+    AWQB_REQUIRE(false, kInvalidArgument, "bad dtype %d", dtype);
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+extern "C" int awqb_moe_topk_sum(const void* in, int64_t M, int64_t topk, int64_t H,
+                                 const int32_t* topk_ids, int64_t e_begin, int64_t e_end, int dtype,
+                                 void* out, void* stream) {
+  AWQB_REQUIRE(M >= 0 && topk >= 1 && H >= 1, kInvalidArgument, "bad sizes");
+  if (M == 0) return kOk;
+  AWQB_REQUIRE(in && out, kInvalidArgument, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned g = grid1d(M * H, 256);
+  if (dtype == AWQB_DTYPE_F16)
+    topk_sum_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(in), (int)M, (int)topk, (int)H,
+                                               topk_ids, (int)e_begin, (int)e_end,
+                                               static_cast<__half*>(out));
+  else if (dtype == AWQB_DTYPE_BF16)
+    topk_sum_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), (int)M,
+                                                      (int)topk, (int)H, topk_ids, (int)e_begin,
+                                                      (int)e_end, static_cast<__nv_bfloat16*>(out));
+  else
+    AWQB_REQUIRE(false, kInvalidArgument, "bad dtype %d", dtype);
+  AWQB_LAUNCH_CHECK();
+  return kOk;
+}

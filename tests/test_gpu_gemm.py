@@ -1,0 +1,119 @@
+"""W4A16 GEMM on the GPU against the fp32-accumulated oracle and against the
+reference Triton kernel's own outputs. Tolerance (task contract):
+max|y - ref| <= 1e-2 * max|ref|."""
+
+import pytest
+import torch
+
+from oracle.awq_ref import awq_linear_ref, dequant_ref, gemm_ref, rel_err
+from sglite_b200 import ops
+from sglite_b200.synthetic import make_activations, make_awq_weights
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _setup(cuda, M, K, N, G, dtype, seed):
+    w = make_awq_weights(K, N, G, dtype, seed=seed)
+    x = make_activations(M, K, dtype, seed=seed + 1)
+    blob = ops.repack(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    return w, x, blob
+
+
+EDGE_M = [1, 3, 16, 17, 63, 64, 65, 127, 200, 257, 511]
+
+
+@pytest.mark.parametrize("M", EDGE_M)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_gemm_edge_m(cuda, M, dtype):
+    K, N, G = 512, 384, 128
+    w, x, blob = _setup(cuda, M, K, N, G, dtype, seed=M)
+    y = ops.gemm(x.to(cuda), blob, K, N, G)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert y.shape == (M, N) and y.dtype == dtype
+    assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("K,N,G", [(256, 136, 32), (320, 256, 64), (1024, 512, 1024), (128, 128, 128),
+                                   (768, 1536, 128), (2048, 768, 128)])
+@pytest.mark.parametrize("M", [1, 33, 300])
+def test_gemm_shapes_and_groups(cuda, K, N, G, M):
+    dtype = torch.bfloat16
+    w, x, blob = _setup(cuda, M, K, N, G, dtype, seed=K + N + M)
+    y = ops.gemm(x.to(cuda), blob, K, N, G)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("ntok", [16, 32, 64, 128, 256])
+@pytest.mark.parametrize("ctas", [1, 3, 7, 64, 0])
+def test_gemm_tiles_and_stream_k_splits(cuda, ntok, ctas):
+    # few CTAs force tiles to be split across contributors and fixed up
+    M, K, N, G = 70, 1024, 512, 128
+    w, x, blob = _setup(cuda, M, K, N, G, torch.float16, seed=ntok * 13 + ctas)
+    y = ops.gemm(x.to(cuda), blob, K, N, G, ntok=ntok, ctas=ctas)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y, ref) <= TOL
+
+
+def test_gemm_bias_and_batch_dims(cuda):
+    M, K, N, G = 6, 256, 256, 128
+    dtype = torch.float16
+    w, x, blob = _setup(cuda, M, K, N, G, dtype, seed=3)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(4)).to(dtype)
+    y = ops.gemm(x.view(2, 3, K).to(cuda), blob, K, N, G, bias=bias.to(cuda))
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G, bias=bias)
+    assert y.shape == (2, 3, N)
+    assert rel_err(y.view(M, N), ref) <= TOL
+
+
+def test_gemm_deterministic_and_workspace_clean(cuda):
+    M, K, N, G = 9, 4096, 4096, 128
+    w, x, blob = _setup(cuda, M, K, N, G, torch.bfloat16, seed=21)
+    xd = x.to(cuda)
+    y1 = ops.gemm(xd, blob, K, N, G)
+    y2 = ops.gemm(xd, blob, K, N, G)
+    assert torch.equal(y1, y2)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y1, ref) <= TOL
+    assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_gemm_vs_reference_kernel_golden(cuda, golden, i):
+    k = f"gemm{i}"
+    M, K, N, G = (int(v) for v in golden[k + "_shape"])
+    x = torch.from_numpy(golden[k + "_x"]).view(torch.float16)
+    qw = torch.from_numpy(golden[k + "_qweight"])
+    qz = torch.from_numpy(golden[k + "_qzeros"])
+    sc = torch.from_numpy(golden[k + "_scales"]).view(torch.float16)
+    y_ref_kernel = torch.from_numpy(golden[k + "_y"]).view(torch.float16)
+    blob = ops.repack(qw.to(cuda), qz.to(cuda), sc.to(cuda), G)
+    y = ops.gemm(x.to(cuda), blob, K, N, G)
+    # the reference kernel accumulates in fp16; both must be within the contract
+    # of the fp32 oracle, and of each other
+    ref = gemm_ref(x, dequant_ref(qw, qz, sc, G))
+    assert rel_err(y, ref) <= TOL
+    assert rel_err(y_ref_kernel, ref) <= TOL
+    assert rel_err(y, y_ref_kernel.float()) <= TOL
+
+
+@pytest.mark.parametrize("name,K,N", [("qkv", 4096, 6144), ("down", 14336, 4096)])
+@pytest.mark.parametrize("M", [1, 64])
+def test_gemm_full_size_linearity(cuda, name, K, N, M):
+    """Full Llama-3-8B sizes: y(a + b) = y(a) + y(b) and a column spot check
+    against the oracle on a slice of output features."""
+    G = 128
+    dtype = torch.bfloat16
+    w, x, blob = _setup(cuda, M, K, N, G, dtype, seed=K + M)
+    xa = x.to(cuda)
+    xb = make_activations(M, K, dtype, seed=K + M + 99).to(cuda)
+    ya = ops.gemm(xa, blob, K, N, G).float()
+    yb = ops.gemm(xb, blob, K, N, G).float()
+    yab = ops.gemm((xa.float() + xb.float()).to(dtype), blob, K, N, G).float()
+    assert rel_err(yab, ya + yb) <= 2 * TOL
+    cols = slice(N - 256, N)
+    Wsl = dequant_ref(w["qweight"][:, (N - 256) // 8:], w["qzeros"][:, (N - 256) // 8:], w["scales"][:, cols], G)
+    ref = gemm_ref(x, Wsl)
+    assert rel_err(ya[:, cols], ref) <= TOL
