@@ -47,18 +47,33 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// Activation tensor map: rows of K 16-bit elements, box = 64 elements x ntok
-// rows, 128-byte swizzle, out-of-range rows/columns read as zero.
-int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, int ntok) {
+// Activation tensor map, 128-byte swizzle, out-of-range elements read as zero.
+// K % 64 == 0: a 3-D view {64, rows, K/64} (strides K*2 and 128 bytes) whose box
+// {64, ntok, atoms} brings a whole stage (atoms x 64 k) in one load; otherwise
+// a 2-D view with box {64, ntok} and one load per 64-wide atom. *is3d reports
+// which.
+int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, int ntok, int atoms, int* is3d) {
   auto enc = tensor_map_encoder();
   AWQB_REQUIRE(enc != nullptr, kCudaError, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {64u, (cuuint32_t)ntok};
-  cuuint32_t estride[2] = {1u, 1u};
-  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(x), gdim, gstride, box,
-                   estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  cuuint32_t estride[3] = {1u, 1u, 1u};
+  CUresult r;
+  if (K % 64 == 0) {
+    cuuint64_t gdim[3] = {64, (cuuint64_t)rows, (cuuint64_t)(K / 64)};
+    cuuint64_t gstride[2] = {(cuuint64_t)K * 2, 128};
+    cuuint32_t box[3] = {64u, (cuuint32_t)ntok, (cuuint32_t)atoms};
+    r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(x), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    *is3d = 1;
+  } else {
+    cuuint64_t gdim[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)K * 2};
+    cuuint32_t box[2] = {64u, (cuuint32_t)ntok};
+    r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(x), gdim, gstride, box, estride,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    *is3d = 0;
+  }
   AWQB_REQUIRE(r == CUDA_SUCCESS, kCudaError, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return kOk;
 }
@@ -70,6 +85,9 @@ int choose_ntok(int64_t M) {
   if (M <= 128) return 128;
   return 256;
 }
+
+// 128-k blocks per pipeline stage of the kernel built for this token tile.
+int stage_blocks(int ntok) { return ntok <= 128 ? 2 : 1; }
 
 struct Plan {
   int ntok, gpb;
@@ -91,15 +109,17 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
                (long long)K, (long long)G);
   AWQB_REQUIRE(N % 8 == 0, kInvalidArgument, "N=%lld is not a multiple of 8", (long long)N);
   AWQB_REQUIRE(M < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31), kUnsupported, "sizes too large");
+  AWQB_REQUIRE((M / 16 + 1) * ((N + 127) / 128) * ((K + 127) / 128) < (1ll << 31), kUnsupported,
+               "problem has too many work units");
   pl->ntok = ntok > 0 ? ntok : choose_ntok(M);
   AWQB_REQUIRE(pl->ntok == 16 || pl->ntok == 32 || pl->ntok == 64 || pl->ntok == 128 ||
                    pl->ntok == 256,
                kInvalidArgument, "token tile %d not built", pl->ntok);
   pl->gpb = groups_per_block((int)G);
   pl->NT = (int)(round_up(N, kBlockN) / kBlockN);
-  pl->KB = (int)(round_up(K, kBlockK) / kBlockK);
+  pl->KB = (int)blob_kblocks(K);
   pl->MT = (int)((M + pl->ntok - 1) / pl->ntok);
-  const int64_t U = (int64_t)pl->MT * pl->NT * pl->KB;
+  const int64_t U = (int64_t)pl->MT * pl->NT * (pl->KB / stage_blocks(pl->ntok));
   int64_t c = ctas > 0 ? ctas : device_sm_count();
   if (c > U) c = U;
   if (c < 1) c = 1;
@@ -170,7 +190,8 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   AWQB_REQUIRE(err != nullptr, kCudaError, "cannot resolve the device error word");
 
   CUtensorMap tm;
-  st = make_x_tensor_map(&tm, x, M, K, pl.ntok);
+  int is3d = 0;
+  st = make_x_tensor_map(&tm, x, M, K, pl.ntok, 2 * stage_blocks(pl.ntok), &is3d);
   if (st != kOk) return st;
 
   GemmParams p{};
@@ -188,6 +209,7 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.ws_cnt = static_cast<int32_t*>(workspace);
   p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
   p.err = err;
+  p.x3d = is3d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, s);
@@ -298,7 +320,8 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   uint32_t* err = device_err_ptr();
   AWQB_REQUIRE(err != nullptr, kCudaError, "cannot resolve the device error word");
   CUtensorMap tm;
-  st = make_x_tensor_map(&tm, x_sorted, rows_max, K, pl.ntok);
+  int is3d = 0;
+  st = make_x_tensor_map(&tm, x_sorted, rows_max, K, pl.ntok, 2 * stage_blocks(pl.ntok), &is3d);
   if (st != kOk) return st;
   GemmParams p{};
   p.blob = static_cast<const uint8_t*>(blobs);
@@ -319,6 +342,7 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   p.ws_cnt = static_cast<int32_t*>(workspace);
   p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
   p.err = err;
+  p.x3d = is3d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, s);

@@ -7,16 +7,24 @@
 //
 // Tile: 128 output features (MMA M, operand A = dequantised weights, K-major)
 //       x NTOK tokens (MMA N, operand B = activations, K-major), fp32
-//       accumulator in TMEM. One pipeline stage is 128 input features.
+//       accumulator in TMEM. One pipeline stage is kSB blocks of 128 input
+//       features: 256 for token tiles <= 128, 128 for the 256-token tile.
 //
-// Warp roles (14 warps):
-//   warp 0        producer: bulk copy of the packed weight block + two TMA
-//                 tile loads of X per stage (128-byte swizzle).
+// Warp roles (22 warps):
+//   warp 0        producer: one bulk copy of the stage's packed weight blocks
+//                 (contiguous in the blob) + one 3-D TMA tile load of X per
+//                 stage (128-byte swizzle).
 //   warp 1        TMEM allocator and single-thread tcgen05.mma issuer.
 //   warps 2..5    epilogue: tcgen05.ld of the accumulator, bias, store (or
 //                 split-K partials and the fix-up of the last contributor).
-//   warps 6..13   dequantisers: packed int4 in shared memory -> fp16/bf16 tile
-//                 in the UMMA 128-byte-swizzle K-major layout.
+//   warps 6..21   dequantisers: packed int4 in shared memory -> fp16/bf16 rows
+//                 written straight into tensor memory (tcgen05.st) as the MMA's
+//                 A operand (token tiles <= 128), or into shared memory in the
+//                 128-byte-swizzle K-major layout (token tile 256, whose
+//                 accumulators fill TMEM). Keeping the dequantised weights out
+//                 of shared memory is what lets decode stream at HBM speed:
+//                 the write + MMA read of a smem copy would cost 4 bytes of
+//                 shared-memory bandwidth per weight.
 //
 // Work partition (stream-K): the (tile, k-block) units of the whole problem are
 // split evenly over the persistent CTAs; a CTA walks its units as segments,
@@ -68,47 +76,96 @@ struct GemmParams {
   int32_t num_valid;            // see row_map
   int32_t M, N, K;
   int32_t NT, KB, MT;           // feature tiles, k-blocks, token tiles (max)
-  float* ws_part;               // [gridDim.x][2][128 * NTOK] fp32 partial tiles
+  float* ws_part;               // [gridDim.x][2][128 rows][NTOK] fp32 partial tiles
   int32_t* ws_cnt;              // [MT * NT] arrival counters, zero between calls
   uint32_t* err;                // device error word
+  int32_t x3d;                  // X tensor map is 3-D {64, rows, K/64}: one load per stage
 };
 
 template <int NTOK, int GPB>
 struct GemmCfg {
-  static constexpr int kThreads = 448;
   static constexpr int kEpiWarp0 = 2;
   static constexpr int kNumEpiWarps = 4;
   static constexpr int kDqWarp0 = 6;
-  static constexpr int kNumDqWarps = 8;
-  static constexpr int kPkBytes = block_bytes_for_gpb(GPB);
-  static constexpr int kPkRegion = (kPkBytes + 1023) / 1024 * 1024;
-  static constexpr int kXAtom = NTOK * 128;          // 64 k x NTOK rows, 128 B rows
-  static constexpr int kXBytes = 2 * kXAtom;
+  static constexpr int kNumDqWarps = 16;              // two groups of 8
+  static constexpr int kDqGroupWarps = 8;
+  static constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);
+  static constexpr bool kATmem = NTOK <= 128;         // operand A (weights) in tensor memory
+  static constexpr int kSB = kATmem ? 2 : 1;           // 128-k blocks per pipeline stage
+  static constexpr int kDqPerStage = kSB == 2 ? 16 : 8;  // dequant warps that work on one stage
+  static constexpr int kPkBytes = block_bytes_for_gpb(GPB);   // one packed block
+  static constexpr int kPkStage = kSB * kPkBytes;             // bytes of one stage's bulk copy
+  static constexpr int kPkRegion = (kPkStage + 1023) / 1024 * 1024;
+  static constexpr int kXAtom = NTOK * 128;           // 64 k x NTOK rows, 128 B rows
+  static constexpr int kXAtoms = 2 * kSB;
+  static constexpr int kXBytes = kXAtoms * kXAtom;
   static constexpr int kLStage = kPkRegion + kXBytes;
-  static constexpr int kWStage = 2 * 16384;          // 128 rows x 128 k, two swizzle atoms
-  static constexpr int kSD = 2;
+  static constexpr int kWStage = kATmem ? 0 : 2 * 16384;  // smem copy of A: 128 rows x 128 k
+  static constexpr int kAStageCols = 64 * kSB;         // TMEM columns of one A stage
   static constexpr int kBudget = 225 * 1024 - 1024 - 512;
-  static constexpr int kSL = cmin(12, (kBudget - kSD * kWStage) / kLStage);
+  static constexpr int kSD = kATmem ? cmin(4, (512 - 2 * NTOK) / kAStageCols) : 2;
+  static constexpr int kSL = cmin(16, (kBudget - kSD * kWStage) / kLStage);
   static constexpr int kSmemBytes = 1024 + kSL * kLStage + kSD * kWStage + 512;
+  static constexpr int kAcol0 = 2 * NTOK;             // TMEM: [0, 2*NTOK) accumulators, then A stages
+  static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK + (kATmem ? kSD * kAStageCols : 0)));
+  static_assert(kSD >= 2, "need two A stages");
+  static_assert(kTmemCols <= 512, "TMEM over capacity");
   static_assert((2 * kSL + 2 * kSD + 5) * 8 + 16 <= 512, "barrier area overflow");
-  static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK));
   static_assert(kSL >= 2, "not enough shared memory for two load stages");
+  static_assert(kSmemBytes <= 232448, "shared memory over the sm_100 per-CTA limit");
   static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "MMA N must be 16..256 step 16");
   static_assert(kPkBytes % 16 == 0, "bulk copy size must be a multiple of 16");
 };
 
 // Owner of unit u when U units are split over C CTAs as [cU/C, (c+1)U/C).
-__device__ __forceinline__ int unit_owner(int64_t u, int64_t U, int64_t C) {
-  return (int)(((u + 1) * C - 1) / U);
+__device__ __forceinline__ int unit_owner(int u, int U, int C) {
+  return (int)((((int64_t)u + 1) * C - 1) / U);
 }
 
+// Ring slot + phase bit, advanced without divisions.
+struct RingPos {
+  int idx = 0;
+  uint32_t phase = 0;
+  template <int S>
+  __device__ __forceinline__ void next() {
+    if (++idx == S) {
+      idx = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Walks (tile, stage) units in order: stage kb fastest, then feature tile nt,
+// then token tile mt.
+struct UnitPos {
+  int u, kb, nt, mt;
+  __device__ __forceinline__ void init(int u0, int KBS, int NT) {
+    u = u0;
+    const int tile = u0 / KBS;
+    kb = u0 - tile * KBS;
+    mt = tile / NT;
+    nt = tile - mt * NT;
+  }
+  __device__ __forceinline__ void next(int KBS, int NT) {
+    ++u;
+    if (++kb == KBS) {
+      kb = 0;
+      if (++nt == NT) {
+        nt = 0;
+        ++mt;
+      }
+    }
+  }
+};
+
 template <typename T, int NTOK, int GPB>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __maxnreg__(80)
 awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
   using Cfg = GemmCfg<NTOK, GPB>;
   using DQ = DqTraits<T>;
   constexpr int SL = Cfg::kSL;
   constexpr int SD = Cfg::kSD;
+  constexpr int SB = Cfg::kSB;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -117,41 +174,42 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   uint8_t* lring = base;
   uint8_t* wring = base + SL * Cfg::kLStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(wring + SD * Cfg::kWStage);
-  // barrier slots
   uint64_t* full_l = bars;             // [SL]  TMA bytes landed
   uint64_t* empty_l = bars + SL;       // [SL]  dequant warps + MMA done with the stage
-  uint64_t* full_d = bars + 2 * SL;    // [SD]  dequantised tile written
-  uint64_t* empty_d = full_d + SD;     // [SD]  MMA done reading the tile
+  uint64_t* full_d = bars + 2 * SL;    // [SD]  dequantised A stage written
+  uint64_t* empty_d = full_d + SD;     // [SD]  MMA done reading the A stage
   uint64_t* acc_full = empty_d + SD;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint64_t* drain = acc_empty + 2;     // [1]
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
-  int* s_flag = const_cast<int*>(reinterpret_cast<volatile int*>(s_tmem + 2));
+  volatile int* s_flag = reinterpret_cast<volatile int*>(s_tmem + 2);  // [2]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- work partition (identical in every role)
+  // ---- work partition (identical in every role; all 32-bit, U < 2^31)
   int MT = p.MT;
   if (p.rows_valid != nullptr) {
     const int rows = *p.rows_valid;
     MT = cmin(MT, (rows + NTOK - 1) / NTOK);
   }
-  const int64_t U = (int64_t)MT * p.NT * p.KB;
+  const int KB = p.KB, NT = p.NT;
+  const int KBS = KB / SB;  // stages per tile (KB is even)
+  const int U = MT * NT * KBS;
   // Never more contributors than units, so every CTA below C owns >= 1 unit.
-  const int64_t C = (int64_t)gridDim.x < U ? (int64_t)gridDim.x : U;
-  const bool has_work = (int64_t)blockIdx.x < C;
-  const int64_t u_begin = has_work ? (int64_t)blockIdx.x * U / C : 0;
-  const int64_t u_end = has_work ? (int64_t)(blockIdx.x + 1) * U / C : 0;
+  const int C = (int)gridDim.x < U ? (int)gridDim.x : U;
+  const bool has_work = (int)blockIdx.x < C;
+  const int u_begin = has_work ? (int)((int64_t)blockIdx.x * U / C) : 0;
+  const int u_end = has_work ? (int)((int64_t)(blockIdx.x + 1) * U / C) : 0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SL; ++i) {
       mbar_init(smem_u32(&full_l[i]), 1);
-      mbar_init(smem_u32(&empty_l[i]), Cfg::kNumDqWarps + 1);
+      mbar_init(smem_u32(&empty_l[i]), Cfg::kDqPerStage + 1);
     }
     for (int i = 0; i < SD; ++i) {
-      mbar_init(smem_u32(&full_d[i]), Cfg::kNumDqWarps);
+      mbar_init(smem_u32(&full_d[i]), Cfg::kDqPerStage);
       mbar_init(smem_u32(&empty_d[i]), 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -160,147 +218,191 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     }
     mbar_init(smem_u32(drain), 1);
     *s_abort = 0;
+    prefetch_tmap(&tmap_x);
     fence_barrier_init();
     fence_proxy_async_smem();
   }
+  __syncthreads();
+
+  // TMEM is allocated off the producer's critical path; every warp but the
+  // producer needs its address (named barrier 2).
+  constexpr int kTmemBarThreads = Cfg::kThreads - 32;
+  uint32_t tmem_base = 0;
   if (warp == 1) {
     tmem_alloc(smem_u32(s_tmem), Cfg::kTmemCols);
     tmem_relinquish();
+    tc_fence_before();
+    named_bar_sync(2, kTmemBarThreads);
+    tc_fence_after();
+    tmem_base = *s_tmem;
+  } else if (warp >= 2) {
+    named_bar_sync(2, kTmemBarThreads);
+    tc_fence_after();
+    tmem_base = *s_tmem;
   }
-  if (warp == 0 && lane == 0) prefetch_tmap(&tmap_x);
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *s_tmem;
+  const uint32_t tmem_a_base = tmem_base + (uint32_t)Cfg::kAcol0;
 
-  if (U == 0 || u_begin >= u_end) {
+  if (!has_work || u_begin >= u_end) {
     // nothing to do for this CTA
   } else if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
-      int64_t it = 0;
-      for (int64_t u = u_begin; u < u_end; ++u, ++it) {
-        const int sl = (int)(it % SL);
-        if (it >= SL) {
-          if (!mbar_wait(smem_u32(&empty_l[sl]), (uint32_t)((it / SL) - 1) & 1u)) {
-            atomicOr(p.err, kErrWaitProducer);
-            *s_abort = 1;
-            break;
-          }
-        }
-        if (*s_abort) break;
-        const int64_t tile = u / p.KB;
-        const int kb = (int)(u - tile * p.KB);
-        const int mt = (int)(tile / p.NT);
-        const int nt = (int)(tile - (int64_t)mt * p.NT);
-        const uint8_t* blob = p.blob;
-        if (p.tile_expert != nullptr) blob += (int64_t)p.tile_expert[mt] * p.blob_stride;
-        const uint8_t* src = blob + ((int64_t)nt * p.KB + kb) * Cfg::kPkBytes;
-        uint8_t* st = lring + sl * Cfg::kLStage;
-        const uint32_t bar = smem_u32(&full_l[sl]);
-        mbar_arrive_expect_tx(bar, Cfg::kPkBytes + Cfg::kXBytes);
-        bulk_g2s(smem_u32(st), src, Cfg::kPkBytes, bar, pol_w);
-        tma_load_2d(smem_u32(st + Cfg::kPkRegion), &tmap_x, kb * kBlockK, mt * NTOK, bar, pol_x);
-        tma_load_2d(smem_u32(st + Cfg::kPkRegion + Cfg::kXAtom), &tmap_x, kb * kBlockK + 64,
-                    mt * NTOK, bar, pol_x);
-      }
-      // Do not leave while copies into this CTA's shared memory are in flight.
-      const int64_t issued = it;
-      for (int64_t j = (issued > SL ? issued - SL : 0); j < issued; ++j) {
-        if (!mbar_wait(smem_u32(&full_l[j % SL]), (uint32_t)(j / SL) & 1u)) {
-          atomicOr(p.err, kErrWaitDrain);
+    // The whole warp runs the loop (so addresses stay warp-uniform and live in
+    // uniform registers); one elected lane issues the copies.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    RingPos st;
+    UnitPos up;
+    up.init(u_begin, KBS, NT);
+    int issued = 0;
+    const uint8_t* blob = p.blob;
+    int blob_mt = -1;
+    for (; up.u < u_end; up.next(KBS, NT)) {
+      if (issued >= SL) {
+        if (!mbar_wait(smem_u32(&empty_l[st.idx]), st.phase ^ 1u)) {
+          if (lane == 0) atomicOr(p.err, kErrWaitProducer);
+          *s_abort = 1;
           break;
         }
+      }
+      if (*s_abort) break;
+      if (p.tile_expert != nullptr && up.mt != blob_mt) {
+        blob = p.blob + (int64_t)p.tile_expert[up.mt] * p.blob_stride;
+        blob_mt = up.mt;
+      }
+      const uint8_t* src = blob + ((int64_t)up.nt * KB + up.kb * SB) * Cfg::kPkBytes;
+      uint8_t* stg = lring + st.idx * Cfg::kLStage;
+      const uint32_t bar = smem_u32(&full_l[st.idx]);
+      if (elect_one()) {
+        mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
+        bulk_g2s(smem_u32(stg), src, Cfg::kPkStage, bar, pol_w);
+        if (p.x3d) {
+          tma_load_3d(smem_u32(stg + Cfg::kPkRegion), &tmap_x, 0, up.mt * NTOK, up.kb * Cfg::kXAtoms, bar,
+                      pol_x);
+        } else {
+#pragma unroll
+          for (int a = 0; a < Cfg::kXAtoms; ++a)
+            tma_load_2d(smem_u32(stg + Cfg::kPkRegion + a * Cfg::kXAtom), &tmap_x,
+                        (up.kb * Cfg::kXAtoms + a) * 64, up.mt * NTOK, bar, pol_x);
+        }
+      }
+      __syncwarp();
+      ++issued;
+      st.next<SL>();
+    }
+    // Do not leave while copies into this CTA's shared memory are in flight:
+    // wait for the completion of the last min(issued, SL) stages.
+    for (int j = 0; j < cmin(issued, SL); ++j) {
+      if (st.idx == 0) st.phase ^= 1u;
+      st.idx = (st.idx == 0 ? SL : st.idx) - 1;
+      if (!mbar_wait(smem_u32(&full_l[st.idx]), st.phase)) {
+        if (lane == 0) atomicOr(p.err, kErrWaitDrain);
+        break;
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_f16(128, NTOK, IsBf16<T>::value ? 1 : 0);
-      int64_t it = 0;
-      int seg = 0;
-      bool ok = true;
-      for (int64_t u = u_begin; u < u_end && ok; ++seg) {
-        const int64_t tile = u / p.KB;
-        const int64_t seg_end = (tile + 1) * p.KB < u_end ? (tile + 1) * p.KB : u_end;
-        const int64_t seg_begin = u;
-        const int buf = seg & 1;
-        if (seg >= 2) {
-          if (!mbar_wait(smem_u32(&acc_empty[buf]), (uint32_t)((seg >> 1) - 1) & 1u)) {
-            atomicOr(p.err, kErrWaitMma);
-            *s_abort = 1;
-            break;
-          }
+    // Warp-wide loop, one elected lane issues tcgen05.mma / commit.
+    constexpr uint32_t idesc = make_idesc_f16(128, NTOK, IsBf16<T>::value ? 1 : 0);
+    // Descriptor of stage 0; other stages and k-steps only move the start
+    // address (bits 0..13, in 16-byte units), which never carries out.
+    const uint64_t adesc0 = make_sw128_kmajor_desc(smem_u32(wring));
+    const uint64_t bdesc0 = make_sw128_kmajor_desc(smem_u32(lring + Cfg::kPkRegion));
+    RingPos sl, sd, acc;
+    int seg = 0;
+    bool ok = true;
+    for (int u = u_begin; u < u_end && ok; ++seg) {
+      const int tile = u / KBS;
+      const int seg_end = cmin((tile + 1) * KBS, u_end);
+      const int seg_begin = u;
+      if (seg >= 2) {
+        if (!mbar_wait(smem_u32(&acc_empty[acc.idx]), acc.phase ^ 1u)) {
+          if (lane == 0) atomicOr(p.err, kErrWaitMma);
+          *s_abort = 1;
+          break;
         }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * NTOK);
-        for (; u < seg_end; ++u, ++it) {
-          const int sl = (int)(it % SL);
-          const int sd = (int)(it % SD);
-          if (!mbar_wait(smem_u32(&full_l[sl]), (uint32_t)(it / SL) & 1u) ||
-              !mbar_wait(smem_u32(&full_d[sd]), (uint32_t)(it / SD) & 1u)) {
-            atomicOr(p.err, kErrWaitMma);
-            *s_abort = 1;
-            ok = false;
-            break;
-          }
-          if (*s_abort) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t w_addr = smem_u32(wring + sd * Cfg::kWStage);
-          const uint32_t x_addr = smem_u32(lring + sl * Cfg::kLStage + Cfg::kPkRegion);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t koff = (uint32_t)((kk & 3) * 32);
-            const uint64_t adesc = make_sw128_kmajor_desc(w_addr + (kk >> 2) * 16384 + koff);
-            const uint64_t bdesc = make_sw128_kmajor_desc(x_addr + (kk >> 2) * Cfg::kXAtom + koff);
-            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (u != seg_begin || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(smem_u32(&empty_d[sd]));
-          tc_commit(smem_u32(&empty_l[sl]));
-        }
-        if (ok) tc_commit(smem_u32(&acc_full[buf]));
       }
-      // Every MMA issued must finish before TMEM is released.
-      tc_commit(smem_u32(drain));
-      if (!mbar_wait(smem_u32(drain), 0)) atomicOr(p.err, kErrWaitDrain);
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)(acc.idx * NTOK);
+      for (; u < seg_end; ++u) {
+        if (!mbar_wait(smem_u32(&full_l[sl.idx]), sl.phase) ||
+            !mbar_wait(smem_u32(&full_d[sd.idx]), sd.phase)) {
+          if (lane == 0) atomicOr(p.err, kErrWaitMma);
+          *s_abort = 1;
+          ok = false;
+          break;
+        }
+        if (*s_abort) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t bd = bdesc0 + (uint64_t)((sl.idx * Cfg::kLStage) >> 4);
+        if (elect_one()) {
+          if constexpr (Cfg::kATmem) {
+            // A stage sd: kAStageCols TMEM columns, 8 per 16-wide k step
+            const uint32_t at = tmem_a_base + (uint32_t)(sd.idx * Cfg::kAStageCols);
+            tc_mma_f16_ts(d_tmem, at, bd, idesc, u != seg_begin ? 1u : 0u);
+#pragma unroll
+            for (int kk = 1; kk < 8 * SB; ++kk) {
+              const uint64_t kx = (uint64_t)((kk >> 2) * (Cfg::kXAtom >> 4) + (kk & 3) * 2);
+              tc_mma_f16_ts(d_tmem, at + (uint32_t)(8 * kk), bd + kx, idesc, 1u);
+            }
+          } else {
+            const uint64_t ad = adesc0 + (uint64_t)((sd.idx * Cfg::kWStage) >> 4);
+            tc_mma_f16(d_tmem, ad, bd, idesc, u != seg_begin ? 1u : 0u);
+#pragma unroll
+            for (int kk = 1; kk < 8 * SB; ++kk) {
+              const uint64_t ka = (uint64_t)((kk >> 2) * (16384 >> 4) + (kk & 3) * 2);
+              const uint64_t kx = (uint64_t)((kk >> 2) * (Cfg::kXAtom >> 4) + (kk & 3) * 2);
+              tc_mma_f16(d_tmem, ad + ka, bd + kx, idesc, 1u);
+            }
+          }
+          tc_commit(smem_u32(&empty_d[sd.idx]));
+          tc_commit(smem_u32(&empty_l[sl.idx]));
+        }
+        __syncwarp();
+        sl.next<SL>();
+        sd.next<SD>();
+      }
+      if (ok && elect_one()) tc_commit(smem_u32(&acc_full[acc.idx]));
+      __syncwarp();
+      acc.next<2>();
     }
+    // Every MMA issued must finish before TMEM is released.
+    if (elect_one()) tc_commit(smem_u32(drain));
+    __syncwarp();
+    if (!mbar_wait(smem_u32(drain), 0) && lane == 0) atomicOr(p.err, kErrWaitDrain);
   } else if (warp >= Cfg::kEpiWarp0 && warp < Cfg::kEpiWarp0 + Cfg::kNumEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int f = q * 32 + lane;            // feature row within the tile
     const int etid = threadIdx.x - Cfg::kEpiWarp0 * 32;
-    int seg = 0;
-    for (int64_t u = u_begin; u < u_end; ++seg) {
-      const int64_t tile = u / p.KB;
-      const int64_t t_begin = tile * p.KB;
-      const int64_t t_end = t_begin + p.KB;
-      const int64_t seg_end = t_end < u_end ? t_end : u_end;
-      const int buf = seg & 1;
-      const int mt = (int)(tile / p.NT);
-      const int nt = (int)(tile - (int64_t)mt * p.NT);
+    RingPos acc;
+    for (int u = u_begin; u < u_end; acc.next<2>()) {
+      const int tile = u / KBS;
+      const int t_begin = tile * KBS;
+      const int t_end = t_begin + KBS;
+      const int seg_end = cmin(t_end, u_end);
+      const int mt = tile / NT;
+      const int nt = tile - mt * NT;
       const int n = nt * kBlockN + f;
       int rows_here = p.M - mt * NTOK;
       if (p.rows_valid != nullptr) rows_here = cmin(rows_here, *p.rows_valid - mt * NTOK);
       rows_here = cmax(0, cmin(NTOK, rows_here));
       const int ncols = (rows_here + 15) & ~15;
 
-      if (!mbar_wait(smem_u32(&acc_full[buf]), (uint32_t)(seg >> 1) & 1u)) {
+      if (!mbar_wait(smem_u32(&acc_full[acc.idx]), acc.phase)) {
         atomicOr(p.err, kErrWaitEpilogue);
         *s_abort = 1;
         break;
       }
       tc_fence_after();
-      const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * NTOK);
+      const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc.idx * NTOK);
       const int c_first = unit_owner(t_begin, U, C);
       const int c_last = unit_owner(t_end - 1, U, C);
-      const bool whole = (c_first == c_last);
 
       float bias_v = 0.f;
       if (p.bias != nullptr && n < p.N) bias_v = (float)reinterpret_cast<const T*>(p.bias)[n];
 
-      if (whole) {
+      if (c_first == c_last) {
+#pragma unroll 1
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(t_addr + c0, v);
@@ -322,52 +424,91 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
       } else {
         // Partial tile: this CTA's slot 0 holds its first segment, slot 1 its last.
+        // Row-major [128][NTOK] so each thread moves its row with 16-byte accesses.
         const int slot = (u == u_begin) ? 0 : 1;
-        float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK);
+        float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK) + f * NTOK;
+#pragma unroll 1
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           uint32_t v[16];
           tmem_ld16(t_addr + c0, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 16; ++c) __stcg(&part[(c0 + c) * 128 + f], __uint_as_float(v[c]));
+          for (int c = 0; c < 16; c += 4)
+            if (c0 + c < rows_here)
+              __stcg(reinterpret_cast<float4*>(part + c0 + c),
+                     make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
+                                 __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])));
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[buf]));
-        __threadfence();
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
+        // Arrive on the tile counter: the block barrier orders every thread's
+        // partial stores before thread 0's release-ordered add (cumulativity).
         named_bar_sync(1, Cfg::kNumEpiWarps * 32);
         if (etid == 0) {
-          const int prev = atomicAdd(&p.ws_cnt[tile], 1);
-          *s_flag = (prev == c_last - c_first) ? 1 : 0;
+          const int prev = atom_add_release_gpu(&p.ws_cnt[tile], 1);
+          const int last = (prev == c_last - c_first) ? 1 : 0;
+          if (last) {
+            fence_acquire_gpu();  // the other contributors' partials
+            p.ws_cnt[tile] = 0;
+          }
+          s_flag[acc.idx] = last;
         }
         named_bar_sync(1, Cfg::kNumEpiWarps * 32);
-        const int last = *s_flag;
-        named_bar_sync(1, Cfg::kNumEpiWarps * 32);  // s_flag may be rewritten next segment
-        if (last) {
-          __threadfence();
-          for (int mloc = 0; mloc < rows_here; ++mloc) {
-            float acc = 0.f;
-            for (int c = c_first; c <= c_last; ++c) {
-              // tile is contributor c's first segment iff c's range starts inside it
-              const int64_t cb = (int64_t)c * U / C;
-              const int cs = (cb >= t_begin) ? 0 : 1;
-              acc += __ldcg(&p.ws_part[((int64_t)c * 2 + cs) * (128 * NTOK) + mloc * 128 + f]);
+        if (s_flag[acc.idx]) {
+          const int ncontrib = c_last - c_first + 1;
+#pragma unroll 1
+          for (int c0 = 0; c0 < rows_here; c0 += 8) {
+            const int nv = cmin(2, (rows_here - c0 + 3) >> 2);  // float4s holding live rows
+            float4 acc4[2];
+            acc4[0] = acc4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            // Contributors in batches of 4 with all loads of a batch in flight
+            // at once; the summation order (contributor order) stays fixed.
+#pragma unroll 1
+            for (int cb = 0; cb < ncontrib; cb += 4) {
+              float4 a[4][2];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int cj = c_first + cb + j;
+                const bool live = cb + j < ncontrib;
+                const int64_t cbeg = (int64_t)cj * U / C;
+                const int cs = (cbeg >= t_begin) ? 0 : 1;
+                const float4* src = reinterpret_cast<const float4*>(
+                    p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK) + f * NTOK + c0);
+#pragma unroll
+                for (int i = 0; i < 2; ++i)
+                  a[j][i] = (live && i < nv) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                  acc4[i].x += a[j][i].x;
+                  acc4[i].y += a[j][i].y;
+                  acc4[i].z += a[j][i].z;
+                  acc4[i].w += a[j][i].w;
+                }
             }
             if (n < p.N) {
-              int m = mt * NTOK + mloc;
-              float val = acc + bias_v;
-              if (p.row_map != nullptr) {
-                m = p.row_map[m];
-                if (m >= p.num_valid) continue;
+              const float* accf = reinterpret_cast<const float*>(acc4);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const int mloc = c0 + c;
+                if (mloc >= rows_here) break;
+                int m = mt * NTOK + mloc;
+                float val = accf[c] + bias_v;
+                if (p.row_map != nullptr) {
+                  m = p.row_map[m];
+                  if (m >= p.num_valid) continue;
+                }
+                if (p.row_scale != nullptr) val *= p.row_scale[m];
+                reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
               }
-              if (p.row_scale != nullptr) val *= p.row_scale[m];
-              reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
             }
           }
-          if (etid == 0) p.ws_cnt[tile] = 0;
         }
       }
       u = seg_end;
@@ -375,61 +516,94 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     tc_fence_before();
   } else if (warp >= Cfg::kDqWarp0) {
     // ------------------------------------------------------------ dequantisers
-    const int d = threadIdx.x - Cfg::kDqWarp0 * 32;  // 0..255
-    const int r = d & 127;                           // weight row (feature) in the tile
-    const int h = d >> 7;                            // which 64-wide half of the stage
+    // Work items are (stage, block) pairs in order; group g of 8 warps takes
+    // items g, g+2, ...: with two blocks per stage each group owns one block of
+    // every stage, with one block per stage the groups alternate stages (so one
+    // group's latencies overlap the other's arithmetic). Warp w writes TMEM
+    // lanes 32*(w%4).. (the hardware restriction), so a thread owns weight row
+    // r = 32*(w%4) + lane and the eight words (64 k) of half h of its block:
+    // two 16-byte shared loads, eight dequantised 16-byte chunks.
+    const int wi = warp - Cfg::kDqWarp0;      // 0..15
+    const int dg = wi >> 3;                   // group 0 / 1
+    const int h = (wi >> 2) & 1;              // 64-wide half of the block
+    const int q = warp & 3;                   // TMEM lane quarter
+    const int r = q * 32 + lane;
     const int rsw = r & 7;
-    int64_t it = 0;
-    for (int64_t u = u_begin; u < u_end; ++u, ++it) {
-      const int sl = (int)(it % SL);
-      const int sd = (int)(it % SD);
-      if (!mbar_wait(smem_u32(&full_l[sl]), (uint32_t)(it / SL) & 1u)) {
+    const int blk = (SB == 2) ? dg : 0;       // block of the stage this group dequantises
+    const int step = 2 / SB;                  // stages between this group's items
+    const uint32_t ld_off = (uint32_t)(blk * Cfg::kPkBytes + ((2 * h * 128 + r) << 4));
+    const uint32_t st_off = (uint32_t)(h * 16384 + r * 128);
+    int il = 0, pl = 0;    // load-ring slot / phase of this group's current stage
+    int id = 0, pd = 0;    // A-ring slot / phase
+    if (SB == 1 && dg == 1) {
+      il = 1 % SL; pl = (1 >= SL);
+      id = 1 % SD; pd = (1 >= SD);
+    }
+    for (int u = u_begin + (SB == 1 ? dg : 0); u < u_end; u += step) {
+      if (!mbar_wait(smem_u32(&full_l[il]), (uint32_t)pl)) {
         atomicOr(p.err, kErrWaitDequant);
         *s_abort = 1;
         break;
       }
-      if (it >= SD) {
-        if (!mbar_wait(smem_u32(&empty_d[sd]), (uint32_t)((it / SD) - 1) & 1u)) {
+      if (u - u_begin >= SD) {
+        if (!mbar_wait(smem_u32(&empty_d[id]), (uint32_t)pd ^ 1u)) {
           atomicOr(p.err, kErrWaitDequant);
           *s_abort = 1;
           break;
         }
       }
       if (*s_abort) break;
-      const uint8_t* pk = lring + sl * Cfg::kLStage;
-      uint8_t* wt = wring + sd * Cfg::kWStage + h * 16384 + r * 128;
+      if constexpr (Cfg::kATmem) tc_fence_after();  // order our TMEM stores after the MMAs that read the slot
+      const uint8_t* pk = lring + il * Cfg::kLStage;
+      const uint8_t* pkb = pk + blk * Cfg::kPkBytes;
       typename DQ::Terms terms[GPB >= 4 ? 2 : 1];
       {
         uint16_t sb;
         uint32_t z;
         if constexpr (GPB >= 4) {
-          block_scale_zero(pk, GPB, 2 * h, r, sb, z);
+          block_scale_zero(pkb, GPB, 2 * h, r, sb, z);
           terms[0] = DQ::make(sb, z);
-          block_scale_zero(pk, GPB, 2 * h + 1, r, sb, z);
+          block_scale_zero(pkb, GPB, 2 * h + 1, r, sb, z);
           terms[1] = DQ::make(sb, z);
         } else {
-          block_scale_zero(pk, GPB, GPB == 2 ? h : 0, r, sb, z);
+          block_scale_zero(pkb, GPB, GPB == 2 ? h : 0, r, sb, z);
           terms[0] = DQ::make(sb, z);
         }
       }
+      const uint4 v0 = *reinterpret_cast<const uint4*>(pk + ld_off);
+      const uint4 v1 = *reinterpret_cast<const uint4*>(pk + ld_off + 128 * 16);
+      const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+      if constexpr (Cfg::kATmem) {
+        uint32_t o[32];
 #pragma unroll
-      for (int jq = 0; jq < 2; ++jq) {
-        const int j4 = 2 * h + jq;
-        const uint4 v = *reinterpret_cast<const uint4*>(pk + ((j4 * 128 + r) << 4));
-        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+        for (int jl = 0; jl < 8; ++jl) {
+          const uint4 t = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
+          o[4 * jl] = t.x;
+          o[4 * jl + 1] = t.y;
+          o[4 * jl + 2] = t.z;
+          o[4 * jl + 3] = t.w;
+        }
+        tmem_st32(tmem_a_base + ((uint32_t)(q * 32) << 16) +
+                      (uint32_t)(id * Cfg::kAStageCols + blk * 64 + h * 32),
+                  o);
+        tmem_st_wait();
+        tc_fence_before();
+      } else {
+        uint8_t* wt = wring + id * Cfg::kWStage + st_off;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int jl = jq * 4 + e;  // word index within this half: 0..7
-          const uint4 o = DQ::dq8(wv[e], terms[GPB >= 4 ? jq : 0]);
+        for (int jl = 0; jl < 8; ++jl) {
+          const uint4 o = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
           *reinterpret_cast<uint4*>(wt + ((jl ^ rsw) << 4)) = o;
         }
+        fence_proxy_async_smem();
       }
-      fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(smem_u32(&full_d[sd]));
-        mbar_arrive(smem_u32(&empty_l[sl]));
+        mbar_arrive(smem_u32(&full_d[id]));
+        mbar_arrive(smem_u32(&empty_l[il]));
       }
+      il += step; if (il >= SL) { il -= SL; pl ^= 1; }
+      id += step; if (id >= SD) { id -= SD; pd ^= 1; }
     }
   }
 

@@ -26,6 +26,9 @@
 //     [.., +64*gpb)        zeros, u32 index g*16 + r/8, nibble 4*(r%8)
 //   gpb = groups per block = 128/G for G in {32, 64}, else 1 (G a multiple of
 //   128: the block holds the single group it lies in).
+//   The number of k-blocks per feature tile is padded to an even count,
+//   KB = 2 * ceil(K / 256), so that the GEMM can stream two blocks (256 k) per
+//   pipeline stage with one bulk copy.
 //   Padding features and padding K carry q = z = 0 and s = 0, i.e. weight 0.
 #pragma once
 #include <cstdint>
@@ -38,6 +41,7 @@ constexpr int kBlockN = 128;        // output features per block / per MMA tile
 constexpr int kBlockK = 128;        // input features per block / per pipeline stage
 constexpr int kWordBytes = 8192;    // packed nibbles of one block
 
+__host__ __device__ constexpr int64_t blob_kblocks(int64_t K) { return 2 * ((K + 2 * kBlockK - 1) / (2 * kBlockK)); }
 __host__ __device__ constexpr int groups_per_block(int G) { return G < kBlockK ? kBlockK / G : 1; }
 __host__ __device__ constexpr int block_bytes_for_gpb(int gpb) { return kWordBytes + 320 * gpb; }
 __host__ __device__ constexpr int scale_off() { return kWordBytes; }

@@ -39,7 +39,7 @@ int make_geo(int64_t K, int64_t N, int64_t G, Geo* g) {
   g->N = N;
   g->G = G;
   g->NT = (int)(rup(N, kBlockN) / kBlockN);
-  g->KB = (int)(rup(K, kBlockK) / kBlockK);
+  g->KB = (int)blob_kblocks(K);
   g->gpb = groups_per_block((int)G);
   g->block_bytes = block_bytes_for_gpb(g->gpb);
   g->blob_bytes = (int64_t)g->NT * g->KB * g->block_bytes;
