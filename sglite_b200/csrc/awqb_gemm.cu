@@ -121,6 +121,13 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   pl->MT = (int)((M + pl->ntok - 1) / pl->ntok);
   const int64_t U = (int64_t)pl->MT * pl->NT * (pl->KB / stage_blocks(pl->ntok));
   int64_t c = ctas > 0 ? ctas : device_sm_count();
+  if (ctas <= 0) {
+    // Larger token tiles make each split tile's partials bigger to reduce:
+    // cap the contributors per tile.
+    const int64_t tiles = (int64_t)pl->MT * pl->NT;
+    const int64_t max_contrib = pl->ntok <= 16 ? 1 << 20 : pl->ntok <= 32 ? 6 : pl->ntok <= 64 ? 4 : 2;
+    if (c > tiles * max_contrib) c = tiles * max_contrib;
+  }
   if (c > U) c = U;
   if (c < 1) c = 1;
   pl->ctas = c;

@@ -92,7 +92,7 @@ struct GemmCfg {
   static constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);
   static constexpr bool kATmem = NTOK <= 128;         // operand A (weights) in tensor memory
   static constexpr int kSB = kATmem ? 2 : 1;           // 128-k blocks per pipeline stage
-  static constexpr int kDqPerStage = kSB == 2 ? 16 : 8;  // dequant warps that work on one stage
+  static constexpr int kDqPerStage = 8;                 // one group of warps dequantises a stage
   static constexpr int kPkBytes = block_bytes_for_gpb(GPB);   // one packed block
   static constexpr int kPkStage = kSB * kPkBytes;             // bytes of one stage's bulk copy
   static constexpr int kPkRegion = (kPkStage + 1023) / 1024 * 1024;
@@ -388,46 +388,124 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       rows_here = cmax(0, cmin(NTOK, rows_here));
       const int ncols = (rows_here + 15) & ~15;
 
-      if (!mbar_wait(smem_u32(&acc_full[acc.idx]), acc.phase)) {
-        atomicOr(p.err, kErrWaitEpilogue);
-        *s_abort = 1;
-        break;
-      }
-      tc_fence_after();
-      const uint32_t t_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc.idx * NTOK);
       const int c_first = unit_owner(t_begin, U, C);
       const int c_last = unit_owner(t_end - 1, U, C);
+      const int ncontrib = c_last - c_first + 1;
+      const bool split = ncontrib > 1;
+      // The owner holds the tile's first unit. The tile runs past its range, so
+      // this is its last segment and the other TMEM accumulator buffer is free.
+      const bool owner = split && c_first == (int)blockIdx.x;
+      const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+      const uint32_t t_addr = tmem_base + lane_off + (uint32_t)(acc.idx * NTOK);
+      const uint32_t t_spare = tmem_base + lane_off + (uint32_t)((acc.idx ^ 1) * NTOK);
+      // Partial of contributor cj (slot 0 = its first segment, 1 = its last).
+      auto part_of = [&](int cj) -> const float* {
+        const int64_t cb = (int64_t)cj * U / C;
+        const int cs = (cb >= t_begin) ? 0 : 1;
+        return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK) + f * NTOK;
+      };
+
+      // Wait for the accumulator. Meanwhile an owner whose peers have all
+      // published their partials sums them (in contributor order) into the spare
+      // TMEM buffer, so the fix-up costs nothing once its own MMAs are done.
+      bool pre = false;
+      {
+        const uint32_t bar = smem_u32(&acc_full[acc.idx]);
+        bool done = mbar_try_wait(bar, acc.phase);
+        const uint64_t t0 = done ? 0 : globaltimer_ns();
+        while (!done) {
+          if (owner && !pre) {
+            // every lane acquires for itself; the decision is warp-uniform
+            if (__all_sync(0xffffffffu, ld_acquire_gpu(&p.ws_cnt[tile]) == ncontrib - 1)) {
+#pragma unroll 1
+              for (int c0 = 0; c0 < rows_here; c0 += 16) {
+                const int nv = cmin(4, (rows_here - c0 + 3) >> 2);
+                float sum[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sum[i] = 0.f;
+#pragma unroll 1
+                for (int cj = c_first + 1; cj <= c_last; ++cj) {
+                  const float4* src = reinterpret_cast<const float4*>(part_of(cj) + c0);
+                  float4 a[4];
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) a[i] = (i < nv) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                  for (int i = 0; i < 4; ++i) {
+                    sum[4 * i] += a[i].x;
+                    sum[4 * i + 1] += a[i].y;
+                    sum[4 * i + 2] += a[i].z;
+                    sum[4 * i + 3] += a[i].w;
+                  }
+                }
+                uint32_t sv[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) sv[i] = __float_as_uint(sum[i]);
+                tmem_st16(t_spare + (uint32_t)c0, sv);
+              }
+              tmem_st_wait();
+              pre = true;
+            }
+          }
+          done = mbar_try_wait_hint(bar, acc.phase, (owner && !pre) ? 1000u : 20000u);
+          if (!done && globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) break;
+        }
+        if (!done) {
+          atomicOr(p.err, kErrWaitEpilogue);
+          *s_abort = 1;
+          break;
+        }
+      }
+      tc_fence_after();
 
       float bias_v = 0.f;
       if (p.bias != nullptr && n < p.N) bias_v = (float)reinterpret_cast<const T*>(p.bias)[n];
+      auto store_row_vals = [&](int c0, const float* vals, int cnt) {
+        if (n >= p.N) return;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          if (c >= cnt) break;
+          const int mloc = c0 + c;
+          if (mloc >= rows_here) break;
+          int m = mt * NTOK + mloc;
+          float val = vals[c] + bias_v;
+          if (p.row_map != nullptr) {
+            m = p.row_map[m];
+            if (m >= p.num_valid) continue;
+          }
+          if (p.row_scale != nullptr) val *= p.row_scale[m];
+          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
+        }
+      };
 
-      if (c_first == c_last) {
+      const bool fast = split && named_bar_and(1, Cfg::kNumEpiWarps * 32, owner && pre);
+      if (!split || fast) {
+        // Whole tile, or an owner with its peers' sum ready: final values now.
 #pragma unroll 1
         for (int c0 = 0; c0 < ncols; c0 += 16) {
           uint32_t v[16];
+          float vals[16];
           tmem_ld16(t_addr + c0, v);
-          tmem_ld_wait();
+          if (fast) {
+            uint32_t w[16];
+            tmem_ld16(t_spare + c0, w);
+            tmem_ld_wait();
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int mloc = c0 + c;
-            if (mloc < rows_here && n < p.N) {
-              int m = mt * NTOK + mloc;
-              float val = __uint_as_float(v[c]) + bias_v;
-              if (p.row_map != nullptr) {
-                m = p.row_map[m];
-                if (m >= p.num_valid) continue;
-              }
-              if (p.row_scale != nullptr) val *= p.row_scale[m];
-              reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
-            }
+            for (int c = 0; c < 16; ++c) vals[c] = __uint_as_float(w[c]) + __uint_as_float(v[c]);
+          } else {
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) vals[c] = __uint_as_float(v[c]);
           }
+          store_row_vals(c0, vals, 16);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
+        if (fast && etid == 0) p.ws_cnt[tile] = 0;  // every peer has arrived; nobody else touches it
       } else {
-        // Partial tile: this CTA's slot 0 holds its first segment, slot 1 its last.
-        // Row-major [128][NTOK] so each thread moves its row with 16-byte accesses.
+        // Publish this CTA's partial: slot 0 holds its first segment, slot 1 its
+        // last. Row-major [128][NTOK] so each thread moves its row with 16-byte
+        // accesses.
         const int slot = (u == u_begin) ? 0 : 1;
         float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK) + f * NTOK;
 #pragma unroll 1
@@ -450,7 +528,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         named_bar_sync(1, Cfg::kNumEpiWarps * 32);
         if (etid == 0) {
           const int prev = atom_add_release_gpu(&p.ws_cnt[tile], 1);
-          const int last = (prev == c_last - c_first) ? 1 : 0;
+          const int last = (prev == ncontrib - 1) ? 1 : 0;
           if (last) {
             fence_acquire_gpu();  // the other contributors' partials
             p.ws_cnt[tile] = 0;
@@ -459,25 +537,22 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         }
         named_bar_sync(1, Cfg::kNumEpiWarps * 32);
         if (s_flag[acc.idx]) {
-          const int ncontrib = c_last - c_first + 1;
+          // Sum in the owner-last order (c_first+1 .. c_last, then c_first) so
+          // the result does not depend on which contributor finished last.
 #pragma unroll 1
           for (int c0 = 0; c0 < rows_here; c0 += 8) {
             const int nv = cmin(2, (rows_here - c0 + 3) >> 2);  // float4s holding live rows
             float4 acc4[2];
             acc4[0] = acc4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-            // Contributors in batches of 4 with all loads of a batch in flight
-            // at once; the summation order (contributor order) stays fixed.
 #pragma unroll 1
             for (int cb = 0; cb < ncontrib; cb += 4) {
               float4 a[4][2];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                const int cj = c_first + cb + j;
-                const bool live = cb + j < ncontrib;
-                const int64_t cbeg = (int64_t)cj * U / C;
-                const int cs = (cbeg >= t_begin) ? 0 : 1;
-                const float4* src = reinterpret_cast<const float4*>(
-                    p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK) + f * NTOK + c0);
+                const int idx = cb + j;
+                const bool live = idx < ncontrib;
+                const int cj = (idx < ncontrib - 1) ? c_first + 1 + idx : c_first;
+                const float4* src = reinterpret_cast<const float4*>(part_of(cj) + c0);
 #pragma unroll
                 for (int i = 0; i < 2; ++i)
                   a[j][i] = (live && i < nv) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -492,22 +567,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
                   acc4[i].w += a[j][i].w;
                 }
             }
-            if (n < p.N) {
-              const float* accf = reinterpret_cast<const float*>(acc4);
-#pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                const int mloc = c0 + c;
-                if (mloc >= rows_here) break;
-                int m = mt * NTOK + mloc;
-                float val = accf[c] + bias_v;
-                if (p.row_map != nullptr) {
-                  m = p.row_map[m];
-                  if (m >= p.num_valid) continue;
-                }
-                if (p.row_scale != nullptr) val *= p.row_scale[m];
-                reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
-              }
-            }
+            store_row_vals(c0, reinterpret_cast<const float*>(acc4), 8);
           }
         }
       }
@@ -516,30 +576,23 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     tc_fence_before();
   } else if (warp >= Cfg::kDqWarp0) {
     // ------------------------------------------------------------ dequantisers
-    // Work items are (stage, block) pairs in order; group g of 8 warps takes
-    // items g, g+2, ...: with two blocks per stage each group owns one block of
-    // every stage, with one block per stage the groups alternate stages (so one
-    // group's latencies overlap the other's arithmetic). Warp w writes TMEM
-    // lanes 32*(w%4).. (the hardware restriction), so a thread owns weight row
-    // r = 32*(w%4) + lane and the eight words (64 k) of half h of its block:
-    // two 16-byte shared loads, eight dequantised 16-byte chunks.
+    // Group g of 8 warps takes stages g, g+2, ...: two stages are dequantised
+    // at once, so one group's load / TMEM-store / barrier latencies overlap the
+    // other group's arithmetic. Warp w writes TMEM lanes 32*(w%4).. (the
+    // hardware restriction), so a thread owns weight row r = 32*(w%4) + lane and,
+    // in every block of its stage, the eight words (64 k) of half h: two 16-byte
+    // shared loads and eight dequantised 16-byte chunks per block.
     const int wi = warp - Cfg::kDqWarp0;      // 0..15
     const int dg = wi >> 3;                   // group 0 / 1
-    const int h = (wi >> 2) & 1;              // 64-wide half of the block
+    const int h = (wi >> 2) & 1;              // 64-wide half of each block
     const int q = warp & 3;                   // TMEM lane quarter
     const int r = q * 32 + lane;
     const int rsw = r & 7;
-    const int blk = (SB == 2) ? dg : 0;       // block of the stage this group dequantises
-    const int step = 2 / SB;                  // stages between this group's items
-    const uint32_t ld_off = (uint32_t)(blk * Cfg::kPkBytes + ((2 * h * 128 + r) << 4));
+    const uint32_t ld_off = (uint32_t)((2 * h * 128 + r) << 4);
     const uint32_t st_off = (uint32_t)(h * 16384 + r * 128);
-    int il = 0, pl = 0;    // load-ring slot / phase of this group's current stage
-    int id = 0, pd = 0;    // A-ring slot / phase
-    if (SB == 1 && dg == 1) {
-      il = 1 % SL; pl = (1 >= SL);
-      id = 1 % SD; pd = (1 >= SD);
-    }
-    for (int u = u_begin + (SB == 1 ? dg : 0); u < u_end; u += step) {
+    int il = dg % SL, pl = (dg >= SL);    // load-ring slot / phase of this group's current stage
+    int id = dg % SD, pd = (dg >= SD);    // A-ring slot / phase
+    for (int u = u_begin + dg; u < u_end; u += 2) {
       if (!mbar_wait(smem_u32(&full_l[il]), (uint32_t)pl)) {
         atomicOr(p.err, kErrWaitDequant);
         *s_abort = 1;
@@ -555,46 +608,52 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       if (*s_abort) break;
       if constexpr (Cfg::kATmem) tc_fence_after();  // order our TMEM stores after the MMAs that read the slot
       const uint8_t* pk = lring + il * Cfg::kLStage;
-      const uint8_t* pkb = pk + blk * Cfg::kPkBytes;
-      typename DQ::Terms terms[GPB >= 4 ? 2 : 1];
-      {
-        uint16_t sb;
-        uint32_t z;
-        if constexpr (GPB >= 4) {
-          block_scale_zero(pkb, GPB, 2 * h, r, sb, z);
-          terms[0] = DQ::make(sb, z);
-          block_scale_zero(pkb, GPB, 2 * h + 1, r, sb, z);
-          terms[1] = DQ::make(sb, z);
+#pragma unroll
+      for (int blk = 0; blk < SB; ++blk) {
+        const uint8_t* pkb = pk + blk * Cfg::kPkBytes;
+        typename DQ::Terms terms[GPB >= 4 ? 2 : 1];
+        {
+          uint16_t sb;
+          uint32_t z;
+          if constexpr (GPB >= 4) {
+            block_scale_zero(pkb, GPB, 2 * h, r, sb, z);
+            terms[0] = DQ::make(sb, z);
+            block_scale_zero(pkb, GPB, 2 * h + 1, r, sb, z);
+            terms[1] = DQ::make(sb, z);
+          } else {
+            block_scale_zero(pkb, GPB, GPB == 2 ? h : 0, r, sb, z);
+            terms[0] = DQ::make(sb, z);
+          }
+        }
+        const uint4 v0 = *reinterpret_cast<const uint4*>(pkb + ld_off);
+        const uint4 v1 = *reinterpret_cast<const uint4*>(pkb + ld_off + 128 * 16);
+        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        if constexpr (Cfg::kATmem) {
+          uint32_t o[32];
+#pragma unroll
+          for (int jl = 0; jl < 8; ++jl) {
+            const uint4 t = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
+            o[4 * jl] = t.x;
+            o[4 * jl + 1] = t.y;
+            o[4 * jl + 2] = t.z;
+            o[4 * jl + 3] = t.w;
+          }
+          tmem_st32(tmem_a_base + ((uint32_t)(q * 32) << 16) +
+                        (uint32_t)(id * Cfg::kAStageCols + blk * 64 + h * 32),
+                    o);
         } else {
-          block_scale_zero(pkb, GPB, GPB == 2 ? h : 0, r, sb, z);
-          terms[0] = DQ::make(sb, z);
+          uint8_t* wt = wring + id * Cfg::kWStage + st_off;
+#pragma unroll
+          for (int jl = 0; jl < 8; ++jl) {
+            const uint4 o = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
+            *reinterpret_cast<uint4*>(wt + ((jl ^ rsw) << 4)) = o;
+          }
         }
       }
-      const uint4 v0 = *reinterpret_cast<const uint4*>(pk + ld_off);
-      const uint4 v1 = *reinterpret_cast<const uint4*>(pk + ld_off + 128 * 16);
-      const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
       if constexpr (Cfg::kATmem) {
-        uint32_t o[32];
-#pragma unroll
-        for (int jl = 0; jl < 8; ++jl) {
-          const uint4 t = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
-          o[4 * jl] = t.x;
-          o[4 * jl + 1] = t.y;
-          o[4 * jl + 2] = t.z;
-          o[4 * jl + 3] = t.w;
-        }
-        tmem_st32(tmem_a_base + ((uint32_t)(q * 32) << 16) +
-                      (uint32_t)(id * Cfg::kAStageCols + blk * 64 + h * 32),
-                  o);
         tmem_st_wait();
         tc_fence_before();
       } else {
-        uint8_t* wt = wring + id * Cfg::kWStage + st_off;
-#pragma unroll
-        for (int jl = 0; jl < 8; ++jl) {
-          const uint4 o = DQ::dq8(wv[jl], terms[GPB >= 4 ? (jl >> 2) : 0]);
-          *reinterpret_cast<uint4*>(wt + ((jl ^ rsw) << 4)) = o;
-        }
         fence_proxy_async_smem();
       }
       __syncwarp();
@@ -602,8 +661,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         mbar_arrive(smem_u32(&full_d[id]));
         mbar_arrive(smem_u32(&empty_l[il]));
       }
-      il += step; if (il >= SL) { il -= SL; pl ^= 1; }
-      id += step; if (id >= SD) { id -= SD; pd ^= 1; }
+      il += 2; if (il >= SL) { il -= SL; pl ^= 1; }
+      id += 2; if (id >= SD) { id -= SD; pd ^= 1; }
     }
   }
 
