@@ -78,6 +78,24 @@ int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int 
                  const void* blob, const void* bias, void* y, void* workspace,
                  int64_t workspace_bytes, int ntok, int64_t ctas, void* stream);
 
+/* GEMM for callers that cannot provide or allocate device memory: a host that
+ * owns every device byte through its own arena, or code that must never call
+ * cudaMalloc (it may run during CUDA graph capture, or on a path that cannot
+ * afford an allocation's implicit synchronisation). No counterpart in the
+ * reference. Same computation and arguments as awqb_gemm minus the workspace:
+ * the split-K scratch is a fixed array inside the library
+ * (awqb_gemm_noalloc_scratch_bytes() = 16 MiB, held by every GPU that loads the
+ * library until the process exits). Problems that need more scratch are
+ * rejected with status 2 and a message; every M <= 64 fits. Nothing is
+ * allocated: the array's device address is looked up once per device by the
+ * first call made with that device current, so make that first call before
+ * any stream capture. All calls share the one array, so calls that can run at
+ * the same time on the GPU (different streams) race and must be serialised by
+ * the caller. */
+int64_t awqb_gemm_noalloc_scratch_bytes(void);
+int awqb_gemm_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                      const void* blob, const void* bias, void* y, void* stream);
+
 /* ------------------------------------------------------------------------
  * MoE (Qwen3-MoE experts). The reference runs dense experts through
  * FusedMoe.forward, srt/model_executor/layers/fused_moe/fused.py:205-233;

@@ -260,6 +260,67 @@ extern "C" int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int6
                    stream);
 }
 
+// ---------------------------------------------------------------------------
+// GEMM without any caller-provided or library-allocated workspace.
+//
+// Some callers have no way to hand this library device memory: a host that
+// manages every device byte through its own arena and does not let plug-ins
+// allocate, or code that must not call cudaMalloc at all because it may run
+// while a CUDA graph is being captured or on a latency-critical path where the
+// implicit synchronisation of an allocation is not acceptable. For them the
+// split-K scratch (tile counters + fp32 partial tiles) lives in a fixed array
+// compiled into this library. Every GPU that loads the library keeps those
+// kNoAllocScratchBytes for the life of the process.
+namespace awqb {
+namespace {
+
+constexpr int64_t kNoAllocScratchBytes = 16ll << 20;  // 16 MiB: every M <= 64 fits
+__device__ __align__(256) uint8_t g_awqb_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array for the current device. The array's name
+// is only a host-side stand-in, so the address is looked up once per device,
+// with that device current, and cached.
+int noalloc_scratch(uint8_t** out) {
+  static uint8_t* ptrs[kMaxDevices] = {};
+  static std::mutex mu;
+  int dev = 0;
+  AWQB_CUDA(cudaGetDevice(&dev));
+  AWQB_REQUIRE(dev >= 0 && dev < kMaxDevices, kUnsupported, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    AWQB_CUDA(cudaGetSymbolAddress(&p, g_awqb_noalloc_scratch));
+    ptrs[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = ptrs[dev];
+  return kOk;
+}
+
+}  // namespace
+}  // namespace awqb
+
+extern "C" int64_t awqb_gemm_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int awqb_gemm_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                                 const void* blob, const void* bias, void* y, void* stream) {
+  Plan pl;
+  int st = make_plan(M, K, N, G, 0, 0, &pl);
+  if (st != kOk) return st;
+  if (M == 0) return kOk;
+  const int64_t need = pl.cnt_bytes + pl.part_bytes;
+  AWQB_REQUIRE(need <= kNoAllocScratchBytes, kUnsupported,
+               "M=%lld K=%lld N=%lld needs %lld bytes of split-K scratch; the no-allocation entry "
+               "point has %lld (every M <= 64 fits). Use awqb_gemm with a workspace instead.",
+               (long long)M, (long long)K, (long long)N, (long long)need, (long long)kNoAllocScratchBytes);
+  uint8_t* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st != kOk) return st;
+  // The array keeps whatever the previous call left; the tile counters must
+  // start at zero (the partial tiles are always written before they are read).
+  AWQB_CUDA(cudaMemsetAsync(scratch, 0, (size_t)pl.cnt_bytes, static_cast<cudaStream_t>(stream)));
+  return gemm_impl(x, M, K, N, G, dtype, blob, bias, y, scratch, kNoAllocScratchBytes, 0, 0, stream);
+}
+
 extern "C" int awqb_device_error(uint32_t* out) {
   AWQB_REQUIRE(out != nullptr, kInvalidArgument, "out is null");
   AWQB_CUDA(cudaDeviceSynchronize());
