@@ -207,3 +207,88 @@ def device_error(clear: bool = True) -> int:
 
 def abi_version() -> int:
     return lib().awqb_abi_version()
+
+
+# ---------------------------------------------------------------- MoE
+def moe_topk_softmax(logits: torch.Tensor, topk: int, renormalize: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    """fp32 softmax over router logits [M, E], top-k weights [M, k] and ids [M, k]."""
+    lg = logits.float().contiguous()
+    dev = _check_cuda(lg)
+    M, E = lg.shape
+    w = torch.empty((M, topk), dtype=torch.float32, device=dev)
+    ids = torch.empty((M, topk), dtype=torch.int32, device=dev)
+    with _DeviceGuard(dev):
+        call("awqb_moe_topk_softmax", _p(lg), M, E, topk, int(bool(renormalize)), _p(w), _p(ids), _stream(dev))
+    return w, ids
+
+
+def moe_max_padded(numel: int, num_experts: int, block_m: int) -> int:
+    return int(lib().awqb_moe_max_padded(numel, num_experts, block_m))
+
+
+def moe_align(topk_ids: torch.Tensor, e_begin: int, e_end: int, block_m: int):
+    """Expert-sorted (token, k) ids padded per expert to block_m; returns
+    (sorted_ids [max_padded], block_expert [max_padded / block_m], num_post_pad [1])."""
+    ids = topk_ids.contiguous()
+    dev = _check_cuda(ids)
+    numel = ids.numel()
+    maxp = moe_max_padded(numel, e_end - e_begin, block_m)
+    sorted_ids = torch.empty(maxp, dtype=torch.int32, device=dev)
+    block_expert = torch.empty((maxp + block_m - 1) // block_m, dtype=torch.int32, device=dev)
+    npp = torch.empty(1, dtype=torch.int32, device=dev)
+    with _DeviceGuard(dev):
+        call("awqb_moe_align", _p(ids), numel, e_begin, e_end, block_m, _p(sorted_ids), maxp,
+             _p(block_expert), _p(npp), _stream(dev))
+    return sorted_ids, block_expert, npp
+
+
+def moe_gather_rows(x: torch.Tensor, sorted_ids: torch.Tensor, num_post_pad: torch.Tensor, topk: int,
+                    numel: int) -> torch.Tensor:
+    dev = _check_cuda(x, sorted_ids, num_post_pad)
+    rows = sorted_ids.numel()
+    K = x.shape[-1]
+    out = torch.empty((rows, K), dtype=x.dtype, device=dev)
+    with _DeviceGuard(dev):
+        call("awqb_moe_gather_rows", _p(x), K, _p(sorted_ids), _p(num_post_pad), numel, topk, rows, _p(out),
+             _stream(dev))
+    return out
+
+
+def moe_grouped_gemm(x_sorted: torch.Tensor, blobs: torch.Tensor, K: int, N: int, G: int,
+                     block_expert: torch.Tensor, num_post_pad: torch.Tensor, block_m: int,
+                     out: torch.Tensor, row_map: Optional[torch.Tensor] = None,
+                     row_scale: Optional[torch.Tensor] = None, num_valid: int = 0) -> torch.Tensor:
+    """Grouped W4A16 GEMM over expert-sorted rows (blobs: [E, blob_bytes])."""
+    dev = _check_cuda(x_sorted, blobs, block_expert, num_post_pad, out)
+    rows = x_sorted.shape[0]
+    nb = c_i64(0)
+    call("awqb_moe_grouped_workspace_bytes", rows, K, N, G, block_m, ctypes.byref(nb))
+    ws = workspace_pool.get(dev, nb.value)
+    with _DeviceGuard(dev):
+        call("awqb_moe_grouped_gemm", _p(x_sorted), rows, K, N, G, _dtype_code(x_sorted.dtype), _p(blobs),
+             blobs.stride(0), _p(block_expert), _p(num_post_pad), block_m, _p(row_map), _p(row_scale),
+             num_valid, _p(out), out.shape[-1], _p(ws), ws.numel(), _stream(dev))
+    return out
+
+
+def silu_and_mul(h: torch.Tensor, rows_dev: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(h[:, :I]) * h[:, I:] in fp32, rounded to h's dtype."""
+    dev = _check_cuda(h)
+    rows, two_i = h.shape
+    I = two_i // 2
+    if out is None:
+        out = torch.empty((rows, I), dtype=h.dtype, device=dev)
+    with _DeviceGuard(dev):
+        call("awqb_silu_and_mul", _p(h), rows, _p(rows_dev), I, _dtype_code(h.dtype), _p(out), _stream(dev))
+    return out
+
+
+def moe_topk_sum(y3: torch.Tensor, M: int, topk: int, topk_ids: Optional[torch.Tensor], e_begin: int,
+                 e_end: int, out: torch.Tensor) -> torch.Tensor:
+    dev = _check_cuda(y3, out)
+    H = y3.shape[-1]
+    with _DeviceGuard(dev):
+        call("awqb_moe_topk_sum", _p(y3), M, topk, H, _p(topk_ids), e_begin, e_end, _dtype_code(y3.dtype),
+             _p(out), _stream(dev))
+    return out

@@ -1,0 +1,118 @@
+"""Host-side checks that need no GPU: the C-ABI library loads and exports every
+declared symbol, argument validation reports errors through status codes, and
+the linear-method boundary mirrors the reference's interface."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from sglite_b200 import _lib
+from sglite_b200.quantization import AWQB200Config, AWQB200LinearMethod, get_quantization_config, select_awq_config
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "awqb200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(awqb_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    names = declared_symbols()
+    assert len(names) >= 25
+    for name in names:
+        assert hasattr(lib, name), name
+    # and the ctypes binding covers exactly the declared API
+    assert set(_lib.EXPORTED) == set(names)
+
+
+def test_abi_version_and_sizes():
+    lib = _lib.lib()
+    assert lib.awqb_abi_version() == 1
+    out = ctypes.c_int64(0)
+    assert lib.awqb_blob_bytes(4096, 4096, 128, ctypes.byref(out)) == 0
+    # 32 feature tiles x 32 k-blocks x (8192 + 320) bytes
+    assert out.value == 32 * 32 * 8512
+    assert lib.awqb_gemm_workspace_bytes(16, 4096, 4096, 128, ctypes.byref(out)) == 0
+    assert out.value > 0
+
+
+@pytest.mark.parametrize("K,N,G,code", [(4096, 4096, 100, 2), (4096, 4100, 128, 1), (4000, 4096, 128, 1)])
+def test_invalid_shapes_return_status_and_message(K, N, G, code):
+    lib = _lib.lib()
+    out = ctypes.c_int64(0)
+    assert lib.awqb_blob_bytes(K, N, G, ctypes.byref(out)) == code
+    assert len(lib.awqb_last_error()) > 0
+    with pytest.raises(ValueError):
+        _lib.check(code)
+
+
+def test_gemm_rejects_bad_arguments_without_touching_the_gpu():
+    lib = _lib.lib()
+    # bad dtype
+    assert lib.awqb_gemm(None, 1, 4096, 4096, 128, 7, None, None, None, None, 0, None) == 1
+    # null pointers
+    assert lib.awqb_gemm(None, 1, 4096, 4096, 128, 1, None, None, None, None, 0, None) == 1
+    # misaligned activations
+    assert lib.awqb_gemm(ctypes.c_void_p(8), 1, 4096, 4096, 128, 1, ctypes.c_void_p(256), None,
+                         ctypes.c_void_p(256), ctypes.c_void_p(256), 1 << 30, None) == 1
+    assert b"16-byte" in lib.awqb_last_error()
+    # workspace too small
+    assert lib.awqb_gemm(ctypes.c_void_p(256), 16, 4096, 4096, 128, 1, ctypes.c_void_p(256), None,
+                         ctypes.c_void_p(256), ctypes.c_void_p(256), 64, None) == 1
+    assert b"workspace too small" in lib.awqb_last_error()
+
+
+def test_config_matches_reference_semantics():
+    cfg = AWQB200Config.from_config({"w_bit": 4, "q_group_size": 128, "zero_point": True})
+    assert cfg.get_name() == "awq_b200" and cfg.pack_factor == 8
+    assert torch.bfloat16 in cfg.get_supported_act_dtypes() and torch.half in cfg.get_supported_act_dtypes()
+    assert cfg.get_min_capability() == 100
+    assert cfg.get_config_filenames() == ["quant_config.json", "quantize_config.json"]
+    with pytest.raises(ValueError):
+        AWQB200Config(8, 128, True)       # only 4-bit (awq.py:19-23)
+    with pytest.raises(ValueError):
+        AWQB200Config(4, 48, True)
+    with pytest.raises(ValueError):
+        AWQB200Config.from_config({"bits": 4})  # missing keys (base_config.py:76-81)
+    assert get_quantization_config("AWQ_B200") is AWQB200Config
+    with pytest.raises(ValueError):
+        get_quantization_config("gptq")
+    assert AWQB200Config.is_awq_b200_compatible({"quant_method": "awq", "bits": 4, "group_size": 64, "zero_point": True})
+    assert not AWQB200Config.is_awq_b200_compatible({"quant_method": "gptq", "bits": 4, "group_size": 64, "zero_point": True})
+    assert isinstance(select_awq_config({"quant_method": "awq", "w_bit": 4, "q_group_size": 128, "zero_point": True}),
+                      AWQB200Config)
+
+
+def test_create_weights_mirrors_awq_tensors_and_attrs():
+    m = AWQB200Config(4, 128, True).get_linear_method()
+    assert isinstance(m, AWQB200LinearMethod)
+    w = m.create_weights(4096, 6144)
+    assert w["qweight"].shape == (4096, 768) and w["qweight"].dtype == torch.int32
+    assert w["qzeros"].shape == (32, 768) and w["qzeros"].dtype == torch.int32
+    assert w["scales"].shape == (32, 6144)
+    for k in ("qweight", "qzeros"):
+        assert (w[k].input_dim, w[k].output_dim, w[k].packed_dim, w[k].pack_factor) == (0, 1, 1, 8)
+    assert (w["scales"].input_dim, w["scales"].output_dim) == (0, 1)
+    assert w["_input_size"] == 4096 and w["_output_size"] == 6144 and w["_group_size"] == 128
+    with pytest.raises(ValueError):
+        m.create_weights(4000, 6144)   # K not a multiple of the group size
+    with pytest.raises(ValueError):
+        m.create_weights(4096, 6100)   # N not a multiple of the pack factor
+    # channel-wise quantisation: group = input size
+    mc = AWQB200Config(4, -1, True).get_linear_method()
+    assert mc.create_weights(1024, 256)["_group_size"] == 1024
+
+
+def test_process_weights_requires_cuda_and_apply_requires_processing():
+    m = AWQB200Config(4, 128, True).get_linear_method()
+    w = m.create_weights(256, 128)
+    with pytest.raises(RuntimeError):
+        m.process_weights_after_loading(w)
+    with pytest.raises(RuntimeError):
+        m.apply_weights(w, torch.zeros(1, 256))

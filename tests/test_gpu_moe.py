@@ -1,0 +1,107 @@
+"""MoE path on the GPU: routing and expert sort against the oracle (exact),
+the whole AWQ expert pipeline against the oracle and the reference's own
+kernels' outputs, expert-parallel partition, and the Qwen3-30B-A3B shape."""
+
+import pytest
+import torch
+
+from oracle.awq_ref import moe_align_ref, moe_ref, rel_err, topk_softmax_ref
+from sglite_b200 import ops
+from sglite_b200.moe import AWQB200MoeBackend, AWQExpertWeights
+from sglite_b200.synthetic import make_activations, make_awq_weights, make_router_logits
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.mark.parametrize("M,E,k", [(1, 128, 8), (37, 128, 8), (300, 16, 4), (5, 8, 2)])
+@pytest.mark.parametrize("renorm", [True, False])
+def test_topk_softmax_matches_oracle(cuda, M, E, k, renorm):
+    lg = make_router_logits(M, E, seed=M + E)
+    w, ids = ops.moe_topk_softmax(lg.to(cuda), k, renorm)
+    w_ref, ids_ref = topk_softmax_ref(lg, k, renorm)
+    assert torch.equal(ids.cpu(), ids_ref)
+    assert torch.allclose(w.cpu(), w_ref, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("M,E,k,bm", [(1, 128, 8, 16), (16, 128, 8, 16), (256, 128, 8, 32), (999, 16, 4, 64)])
+@pytest.mark.parametrize("ep", [None, (4, 12)])
+def test_align_matches_oracle_exactly(cuda, M, E, k, bm, ep):
+    ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(i))[:k] for i in range(M)]).to(torch.int32)
+    e0, e1 = ep if ep is not None else (0, E)
+    sorted_ids, block_expert, npp = ops.moe_align(ids.to(cuda), e0, e1, bm)
+    s_ref, b_ref, n_ref = moe_align_ref(ids, bm, e0, e1)
+    n = int(npp.item())
+    assert n == n_ref
+    assert torch.equal(sorted_ids[:n].cpu(), s_ref)
+    assert torch.equal(block_expert[: n // bm].cpu(), b_ref)
+    assert (sorted_ids[n:] == ids.numel()).all()  # unused tail carries the sentinel
+
+
+def _experts(E, H, I, G, dtype, seed, cuda):
+    w1 = make_awq_weights(H, 2 * I, G, dtype, seed=seed, batch=E)
+    w2 = make_awq_weights(I, H, G, dtype, seed=seed + 1, batch=E)
+    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    e2 = AWQExpertWeights.from_awq(*(w2[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    return w1, w2, e1, e2
+
+
+@pytest.mark.parametrize("M", [1, 7, 64, 300])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_moe_pipeline_matches_oracle(cuda, M, dtype):
+    E, k, H, I, G = 16, 4, 256, 128, 128
+    w1, w2, e1, e2 = _experts(E, H, I, G, dtype, 11, cuda)
+    x = make_activations(M, H, dtype, seed=M)
+    lg = make_router_logits(M, E, seed=M + 1)
+    y = AWQB200MoeBackend().forward(x.to(cuda).clone(), e1, e2, lg.to(cuda), k, True)
+    ref = moe_ref(x, w1, w2, lg, k, True, G)
+    assert rel_err(y, ref.float()) <= TOL
+
+
+def test_moe_expert_parallel_sum_equals_full(cuda):
+    E, k, H, I, G, M = 16, 4, 256, 128, 128, 40
+    dtype = torch.bfloat16
+    w1 = make_awq_weights(H, 2 * I, G, dtype, seed=5, batch=E)
+    w2 = make_awq_weights(I, H, G, dtype, seed=6, batch=E)
+    x = make_activations(M, H, dtype, seed=7).to(cuda)
+    lg = make_router_logits(M, E, seed=8).to(cuda)
+    parts = []
+    for e0, e1_ in ((0, 8), (8, 16)):
+        sl = slice(e0, e1_)
+        a = AWQExpertWeights.from_awq(*(w1[k_][sl].to(cuda) for k_ in ("qweight", "qzeros", "scales")), G, e0, E)
+        b = AWQExpertWeights.from_awq(*(w2[k_][sl].to(cuda) for k_ in ("qweight", "qzeros", "scales")), G, e0, E)
+        parts.append(AWQB200MoeBackend().forward(x.clone(), a, b, lg, k, True).float())
+    ref = moe_ref(x.cpu(), w1, w2, lg.cpu(), k, True, G)
+    assert rel_err(parts[0] + parts[1], ref.float()) <= TOL
+    # each rank on its own matches the oracle restricted to its experts
+    ref0 = moe_ref(x.cpu(), w1, w2, lg.cpu(), k, True, G, 0, 8)
+    assert rel_err(parts[0], ref0.float()) <= TOL
+
+
+def test_moe_matches_reference_kernels_golden(cuda, golden):
+    E, topk, H, I, M, BM, G = (int(v) for v in golden["moe_shape"])
+    w1 = {k: torch.from_numpy(golden["moe_w1_" + k]) for k in ("qweight", "qzeros", "scales")}
+    w2 = {k: torch.from_numpy(golden["moe_w2_" + k]) for k in ("qweight", "qzeros", "scales")}
+    w1["scales"] = w1["scales"].view(torch.float16)
+    w2["scales"] = w2["scales"].view(torch.float16)
+    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    e2 = AWQExpertWeights.from_awq(*(w2[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    x = torch.from_numpy(golden["moe_x"]).view(torch.float16)
+    lg = torch.from_numpy(golden["moe_logits"])
+    y = AWQB200MoeBackend().forward(x.to(cuda).clone(), e1, e2, lg.to(cuda), topk, True)
+    y_kernel = torch.from_numpy(golden["moe_y"]).view(torch.float16)
+    assert rel_err(y, y_kernel.float()) <= TOL
+
+
+@pytest.mark.parametrize("M", [16, 256])
+def test_qwen3_30b_a3b_moe_shape(cuda, M):
+    E, k, H, I, G = 128, 8, 2048, 768, 128
+    dtype = torch.bfloat16
+    w1, w2, e1, e2 = _experts(E, H, I, G, dtype, 21, cuda)
+    x = make_activations(M, H, dtype, seed=M)
+    lg = make_router_logits(M, E, seed=M + 3)
+    y = AWQB200MoeBackend().forward(x.to(cuda).clone(), e1, e2, lg.to(cuda), k, True)
+    ref = moe_ref(x, w1, w2, lg, k, True, G)
+    assert rel_err(y, ref.float()) <= TOL
+    assert ops.device_error() == 0
