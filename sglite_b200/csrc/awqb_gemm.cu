@@ -136,8 +136,12 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   return kOk;
 }
 
+// pdl: launch as a programmatic dependent of the previous kernel in the stream
+// (the kernel waits for it before touching any data it may have written).
+// Not used for the grouped path, whose row count comes from the previous kernel
+// and is read at kernel start.
 template <typename T, int NTOK, int GPB>
-int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, cudaStream_t stream) {
+int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, bool pdl, cudaStream_t stream) {
   using Cfg = GemmCfg<NTOK, GPB>;
   auto kern = awq_gemm_kernel<T, NTOK, GPB>;
   static bool attr_set[kMaxDevices] = {};
@@ -147,30 +151,39 @@ int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, cudaStrea
     AWQB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_set[dev] = true;
   }
-  kern<<<dim3((unsigned)ctas), dim3(Cfg::kThreads), Cfg::kSmemBytes, stream>>>(tm, p);
-  AWQB_LAUNCH_CHECK();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)ctas);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  AWQB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, p));
   return kOk;
 }
 
 template <typename T, int NTOK>
-int launch_g(const CUtensorMap& tm, const GemmParams& p, int gpb, int64_t ctas, cudaStream_t s) {
+int launch_g(const CUtensorMap& tm, const GemmParams& p, int gpb, int64_t ctas, bool pdl, cudaStream_t s) {
   switch (gpb) {
-    case 1: return launch_t<T, NTOK, 1>(tm, p, ctas, s);
-    case 2: return launch_t<T, NTOK, 2>(tm, p, ctas, s);
-    case 4: return launch_t<T, NTOK, 4>(tm, p, ctas, s);
+    case 1: return launch_t<T, NTOK, 1>(tm, p, ctas, pdl, s);
+    case 2: return launch_t<T, NTOK, 2>(tm, p, ctas, pdl, s);
+    case 4: return launch_t<T, NTOK, 4>(tm, p, ctas, pdl, s);
   }
   AWQB_REQUIRE(false, kUnsupported, "groups per block %d not built", gpb);
   return kUnsupported;
 }
 
 template <typename T>
-int launch_n(const CUtensorMap& tm, const GemmParams& p, const Plan& pl, cudaStream_t s) {
+int launch_n(const CUtensorMap& tm, const GemmParams& p, const Plan& pl, bool pdl, cudaStream_t s) {
   switch (pl.ntok) {
-    case 16: return launch_g<T, 16>(tm, p, pl.gpb, pl.ctas, s);
-    case 32: return launch_g<T, 32>(tm, p, pl.gpb, pl.ctas, s);
-    case 64: return launch_g<T, 64>(tm, p, pl.gpb, pl.ctas, s);
-    case 128: return launch_g<T, 128>(tm, p, pl.gpb, pl.ctas, s);
-    case 256: return launch_g<T, 256>(tm, p, pl.gpb, pl.ctas, s);
+    case 16: return launch_g<T, 16>(tm, p, pl.gpb, pl.ctas, pdl, s);
+    case 32: return launch_g<T, 32>(tm, p, pl.gpb, pl.ctas, pdl, s);
+    case 64: return launch_g<T, 64>(tm, p, pl.gpb, pl.ctas, pdl, s);
+    case 128: return launch_g<T, 128>(tm, p, pl.gpb, pl.ctas, pdl, s);
+    case 256: return launch_g<T, 256>(tm, p, pl.gpb, pl.ctas, pdl, s);
   }
   AWQB_REQUIRE(false, kUnsupported, "token tile %d not built", pl.ntok);
   return kUnsupported;
@@ -218,8 +231,8 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.err = err;
   p.x3d = is3d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
-  return launch_n<__nv_bfloat16>(tm, p, pl, s);
+  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);
+  return launch_n<__nv_bfloat16>(tm, p, pl, true, s);
 }
 
 }  // namespace
@@ -412,6 +425,6 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   p.err = err;
   p.x3d = is3d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, s);
-  return launch_n<__nv_bfloat16>(tm, p, pl, s);
+  if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, false, s);
+  return launch_n<__nv_bfloat16>(tm, p, pl, false, s);
 }

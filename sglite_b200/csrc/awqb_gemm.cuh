@@ -223,6 +223,10 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     fence_proxy_async_smem();
   }
   __syncthreads();
+  // The next GEMM in the stream may start its own set-up and weight streaming
+  // on SMs this grid leaves; it waits (grid_dep_wait) before touching data this
+  // grid writes.
+  grid_dep_launch();
 
   // TMEM is allocated off the producer's critical path; every warp but the
   // producer needs its address (named barrier 2).
@@ -256,6 +260,28 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     int issued = 0;
     const uint8_t* blob = p.blob;
     int blob_mt = -1;
+    // Weights do not depend on the previous kernel in the stream: the first
+    // stages' weight copies go out before waiting for it, their activations
+    // after (each stage's barrier expects both).
+    const int early = cmin(SL, u_end - u_begin);
+    {
+      UnitPos ue = up;
+      for (int j = 0; j < early; ++j, ue.next(KBS, NT)) {
+        if (p.tile_expert != nullptr) {
+          // expert ids are written by the routing kernel: wait before reading them
+          break;
+        }
+        const uint8_t* src = blob + ((int64_t)ue.nt * KB + ue.kb * SB) * Cfg::kPkBytes;
+        const uint32_t bar = smem_u32(&full_l[j]);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
+          bulk_g2s(smem_u32(lring + j * Cfg::kLStage), src, Cfg::kPkStage, bar, pol_w);
+        }
+        __syncwarp();
+      }
+    }
+    const bool weights_early = (p.tile_expert == nullptr);
+    grid_dep_wait();
     for (; up.u < u_end; up.next(KBS, NT)) {
       if (issued >= SL) {
         if (!mbar_wait(smem_u32(&empty_l[st.idx]), st.phase ^ 1u)) {
@@ -272,9 +298,12 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       const uint8_t* src = blob + ((int64_t)up.nt * KB + up.kb * SB) * Cfg::kPkBytes;
       uint8_t* stg = lring + st.idx * Cfg::kLStage;
       const uint32_t bar = smem_u32(&full_l[st.idx]);
+      const bool weights_sent = weights_early && issued < early;
       if (elect_one()) {
-        mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
-        bulk_g2s(smem_u32(stg), src, Cfg::kPkStage, bar, pol_w);
+        if (!weights_sent) {
+          mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
+          bulk_g2s(smem_u32(stg), src, Cfg::kPkStage, bar, pol_w);
+        }
         if (p.x3d) {
           tma_load_3d(smem_u32(stg + Cfg::kPkRegion), &tmap_x, 0, up.mt * NTOK, up.kb * Cfg::kXAtoms, bar,
                       pol_x);
@@ -374,6 +403,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int f = q * 32 + lane;            // feature row within the tile
     const int etid = threadIdx.x - Cfg::kEpiWarp0 * 32;
+    grid_dep_wait();  // outputs, workspace counters and partials belong to the previous grid until then
     RingPos acc;
     for (int u = u_begin; u < u_end; acc.next<2>()) {
       const int tile = u / KBS;

@@ -289,6 +289,12 @@ __device__ __forceinline__ void fence_acquire_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
+// Programmatic dependent launch: wait until the preceding grid in the stream
+// has completed and its memory is visible (a no-op without a programmatic
+// dependency), and allow the dependent grid to be scheduled.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
