@@ -369,6 +369,186 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------- other configs
+def _graph_us(fn, warm, steps, reps=4):
+    """Time of one fn() from graph replays of reps back-to-back calls (the graph
+    launch itself is amortised over reps)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            fn()
+    for _ in range(warm):
+        g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (steps * reps)
+    del g
+    return us
+
+
+def _peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def _linear(K, N, dev, dtype, seed):
+    from sglite_b200.quantization import AWQB200Config
+
+    m = AWQB200Config(4, G, True).get_linear_method()
+    w = m.create_weights(K, N)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w["qweight"] = torch.randint(-2**31, 2**31 - 1, (K, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
+    w["qzeros"] = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
+    w["scales"] = (torch.rand((K // G, N), generator=g, device=dev) * 9e-3 + 1e-3).to(dtype)
+    return m, m.process_weights_after_loading(w)
+
+
+def run_prefill(args):
+    """Config 2: Qwen3-4B AWQ projections at M = 512, 2048, 8192 (fp16)."""
+    from sglite_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    shapes = {"qkv": (2560, 6144), "o": (4096, 2560), "gate_up": (2560, 19456), "down": (9728, 2560)}
+    hbm, tflops_peak, kind = _peaks()
+    rows = {}
+    tot_flop = tot_us = 0.0
+    for i, (n, (K, N)) in enumerate(shapes.items()):
+        _, w = _linear(K, N, dev, torch.float16, i)
+        for M in (512, 2048, 8192):
+            x = torch.randn((M, K), device=dev).to(torch.float16)
+            y = torch.empty((M, N), device=dev, dtype=torch.float16)
+            us = _graph_us(lambda: ops.gemm(x, w["qweight"], K, N, G, out=y), args.warmup, args.steps)
+            fl = 2.0 * M * N * K
+            rows[f"{n}@M{M}"] = {"us": round(us, 2), "tflops": round(fl / us / 1e6, 1),
+                                 "frac": round(fl / us / 1e6 / tflops_peak, 3)}
+            tot_flop += fl
+            tot_us += us
+    print(json.dumps({"workload": "qwen3_4b_awq_prefill (config 2)", "metric": "W4A16 GEMM TFLOP/s",
+                      "value": tot_flop / tot_us / 1e6, "unit": "TFLOP/s", "peak": tflops_peak, "peak_kind": kind,
+                      "frac": tot_flop / tot_us / 1e6 / tflops_peak, "per_gemm": rows, "dtype": "fp16"}), flush=True)
+
+
+def run_single(args):
+    """Config 0: one K=N=4096 projection at M=16 (fp16)."""
+    from sglite_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    K = N = 4096
+    M = 16
+    _, w = _linear(K, N, dev, torch.float16, 0)
+    x = torch.randn((M, K), device=dev).to(torch.float16)
+    y = torch.empty((M, N), device=dev, dtype=torch.float16)
+    us = _graph_us(lambda: ops.gemm(x, w["qweight"], K, N, G, out=y), args.warmup, args.steps)
+    hbm, _, kind = _peaks()
+    b = algo_bytes(M, K, N)
+    print(json.dumps({"workload": "single K=N=4096 M=16 (config 0)", "metric": "GEMM us", "value": us,
+                      "unit": "us", "weight_GBps": awq_bytes(K, N) / us / 1e3, "algo_GBps": b / us / 1e3,
+                      "frac_hbm": b / us / 1e3 / hbm, "peak_kind": kind}), flush=True)
+
+
+def run_tp70b(args):
+    """Config 3: Llama-3.1-70B layer projections under TP=N, all-reduce after O and down."""
+    import torch.distributed as dist
+
+    from sglite_b200 import ops
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    comm = None
+    if world > 1:
+        from datetime import timedelta
+
+        from sglite_b200.distributed import init_nccl
+
+        dist.init_process_group("gloo", timeout=timedelta(seconds=120))
+        comm = init_nccl(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
+                         max_size_bytes=256 * 8192 * 2)
+    full = {"qkv": (8192, 10240), "o": (8192, 8192), "gate_up": (8192, 57344), "down": (28672, 8192)}
+    loc = {n: ((K // world, N) if n in ROW_PARALLEL else (K, N // world)) for n, (K, N) in full.items()}
+    ws = {}
+    for i, (n, (K, N)) in enumerate(loc.items()):
+        _, ws[n] = _linear(K, N, dev, DTYPE, 100 * rank + i)
+    hbm, tflops_peak, kind = _peaks()
+    out = {}
+    for M in (1, 32, 256, 4096):
+        xs = {n: torch.randn((M, K), device=dev).to(DTYPE) for n, (K, N) in loc.items()}
+        ys = {n: torch.empty((M, N), device=dev, dtype=DTYPE) for n, (K, N) in loc.items()}
+
+        def layer():
+            for n, (K, N) in loc.items():
+                ops.gemm(xs[n], ws[n]["qweight"], K, N, G, out=ys[n])
+                if comm is not None and n in ROW_PARALLEL:
+                    comm.all_reduce(ys[n])
+
+        if world > 1:
+            dist.barrier()
+        us = _graph_us(layer, args.warmup, args.steps)
+        if world > 1:
+            t = torch.tensor([us], dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        wbytes = sum(awq_bytes(K, N) for K, N in loc.values())
+        flops = sum(2.0 * M * K * N for K, N in loc.values())
+        ring = 2 * (world - 1) / world * M * 8192 * 2 if world > 1 else 0.0
+        roof_us = max(wbytes / hbm / 1e3, flops / tflops_peak / 1e6) + 2 * ring / 770e3
+        out[f"M{M}"] = {"layer_us": round(us, 2), "roofline_us": round(roof_us, 2), "ratio": round(us / roof_us, 2)}
+    if rank == 0:
+        print(json.dumps({"workload": f"llama3.1_70b_awq_layer_tp{world} (config 3)", "metric": "TP-layer us",
+                          "unit": "us", "n_gpus": world, "per_m": out,
+                          "roofline": "max(weight bytes / measured HBM, flops / measured bf16 peak) + 2 ring all-reduces at 770 GB/s",
+                          "peak_kind": kind}), flush=True)
+    if comm is not None:
+        comm.destroy()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_moe(args):
+    """Config 4: Qwen3-30B-A3B AWQ MoE layer at M = 16, 256, 4096."""
+    from sglite_b200.moe import AWQB200MoeBackend, AWQExpertWeights
+
+    dev = torch.device("cuda", 0)
+    E, k, H, I = 128, 8, 2048, 768
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def experts(K, N):
+        qw = torch.randint(-2**31, 2**31 - 1, (E, K, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
+        qz = torch.randint(-2**31, 2**31 - 1, (E, K // G, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
+        sc = (torch.rand((E, K // G, N), generator=g, device=dev) * 9e-3 + 1e-3).to(DTYPE)
+        return AWQExpertWeights.from_awq(qw, qz, sc, G)
+
+    w1, w2 = experts(H, 2 * I), experts(I, H)
+    backend = AWQB200MoeBackend()
+    hbm, tflops_peak, kind = _peaks()
+    per = {}
+    for M in (16, 256, 4096):
+        x = torch.randn((M, H), device=dev).to(DTYPE)
+        lg = torch.randn((M, E), device=dev)
+        buf = x.clone()
+        us = _graph_us(lambda: backend.forward(buf, w1, w2, lg, k, True), args.warmup, args.steps)
+        _, ids = torch.topk(lg, k, dim=-1)
+        touched = int(torch.unique(ids).numel())
+        wbytes = touched * (awq_bytes(H, 2 * I) + awq_bytes(I, H))
+        flops = 2.0 * M * k * (H * 2 * I + I * H)
+        per[f"M{M}"] = {"us": round(us, 2), "experts_touched": touched, "weight_GBps": round(wbytes / us / 1e3, 1),
+                        "tflops": round(flops / us / 1e6, 1)}
+    print(json.dumps({"workload": "qwen3_30b_a3b_awq_moe (config 4)", "metric": "MoE layer us", "unit": "us",
+                      "per_m": per, "peak_hbm_GBps": hbm, "peak_tflops": tflops_peak, "peak_kind": kind}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -376,11 +556,21 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe"],
+                    help="decode (default, the contract line) or another BASELINE config")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
+    elif args.workload == "single":
+        run_single(args)
+    elif args.workload == "tp70b":
+        run_tp70b(args)
+    elif args.workload == "moe":
+        run_moe(args)
     else:
         run_ours(args)
 

@@ -78,11 +78,15 @@ int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, i
   return kOk;
 }
 
+// Token tile: the smallest built tile that holds a decode batch; 128 (weights
+// in TMEM, 256-k stages) up to a few thousand tokens, where it keeps more tiles
+// in flight than SMs; 256 (weights in shared memory, each dequantised weight
+// reused by twice as many tokens) for the largest prefill batches.
 int choose_ntok(int64_t M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 64) return 64;
-  if (M <= 128) return 128;
+  if (M <= 3072) return 128;
   return 256;
 }
 

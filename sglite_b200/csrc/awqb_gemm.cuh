@@ -489,21 +489,39 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
 
       float bias_v = 0.f;
       if (p.bias != nullptr && n < p.N) bias_v = (float)reinterpret_cast<const T*>(p.bias)[n];
+      // Stores rows c0 .. c0+cnt-1 of this thread's feature. The output row of
+      // each (row_map) and its scale (row_scale) are read once per chunk by
+      // lanes 0..15 and broadcast with shuffles (warp-uniform loop).
       auto store_row_vals = [&](int c0, const float* vals, int cnt) {
-        if (n >= p.N) return;
+        if (p.row_map == nullptr && p.row_scale == nullptr) {  // dense GEMM: rows in order
+          if (n >= p.N) return;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c >= cnt || c0 + c >= rows_here) break;
+            reinterpret_cast<T*>(p.y)[(int64_t)(mt * NTOK + c0 + c) * p.ldy + n] = (T)(vals[c] + bias_v);
+          }
+          return;
+        }
+        const int li = lane & 15;
+        int my_m = mt * NTOK + c0 + li;
+        float my_s = 1.f;
+        bool my_ok = li < cnt && c0 + li < rows_here;
+        if (my_ok && p.row_map != nullptr) {
+          my_m = p.row_map[my_m];
+          my_ok = my_m < p.num_valid;
+        }
+        if (my_ok && p.row_scale != nullptr) my_s = p.row_scale[my_m];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           if (c >= cnt) break;
-          const int mloc = c0 + c;
-          if (mloc >= rows_here) break;
-          int m = mt * NTOK + mloc;
-          float val = vals[c] + bias_v;
-          if (p.row_map != nullptr) {
-            m = p.row_map[m];
-            if (m >= p.num_valid) continue;
+          const int m = __shfl_sync(0xffffffffu, my_m, c);
+          const float sc = __shfl_sync(0xffffffffu, my_s, c);
+          const bool ok = __shfl_sync(0xffffffffu, my_ok ? 1 : 0, c) != 0;
+          if (ok && n < p.N) {
+            float val = vals[c] + bias_v;
+            if (p.row_scale != nullptr) val *= sc;
+            reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
           }
-          if (p.row_scale != nullptr) val *= p.row_scale[m];
-          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
         }
       };
 

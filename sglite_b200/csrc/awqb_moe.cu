@@ -21,6 +21,8 @@ namespace awqb {
 namespace {
 
 constexpr int kMaxExperts = 512;
+
+__device__ __forceinline__ int cmin_i(int a, int b) { return a < b ? a : b; }
 constexpr int kMaxTopk = 32;
 
 // One warp per token. Top-k is chosen on the logits (softmax is monotonic),
@@ -100,17 +102,40 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
     if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < E; ++e) {
-      off[e] = run;
+  // Padded size of every expert (one thread per expert), then an exclusive
+  // prefix sum over experts: a shuffle scan inside each warp of 32 experts and
+  // a short serial pass over the (at most 16) warp totals.
+  int32_t* wsum = off + E + 1;  // [32] per-warp totals of the expert scan
+  for (int e0 = 0; e0 < E; e0 += blockDim.x) {
+    const int e = e0 + threadIdx.x;
+    int padded = 0;
+    if (e < E) {
       int tot = 0;
       for (int w = 0; w < 32; ++w) tot += cnt[w * E + e];
-      run += (tot + block_m - 1) / block_m * block_m;
+      padded = (tot + block_m - 1) / block_m * block_m;
     }
-    off[E] = run;
-    *num_post_pad = run;
+    int incl = padded;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int run = e0 == 0 ? 0 : off[e0];
+      for (int w = 0; w < 32 && e0 + w * 32 < E; ++w) {
+        const int t = wsum[w];
+        wsum[w] = run;
+        run += t;
+      }
+      off[cmin_i(E, e0 + (int)blockDim.x)] = run;
+    }
+    __syncthreads();
+    if (e < E) off[e] = wsum[warp] + incl - padded;
+    __syncthreads();
   }
+  if (threadIdx.x == 0) *num_post_pad = off[E];
   __syncthreads();
   // per-warp write bases: off[e] + counts of lower warps
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -160,41 +185,63 @@ __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* _
 template <typename T>
 __device__ __forceinline__ float to_f(T v) { return (float)v; }
 
-// out[r, j] = silu(in[r, j]) * in[r, I + j], computed in fp32.
+// out[r, j] = silu(in[r, j]) * in[r, I + j], computed in fp32; eight
+// elements (16 bytes) per thread and iteration (I % 8 == 0).
 template <typename T>
 __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
                                     const int32_t* __restrict__ rows_dev, int I, T* __restrict__ out) {
   int64_t rows = rows_max;
   if (rows_dev != nullptr && (int64_t)*rows_dev < rows) rows = *rows_dev;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * I;
+  const int iv = I / 8;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * iv;
        t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / I;
-    const int j = (int)(t - r * I);
-    const float g = to_f(in[r * 2 * I + j]);
-    const float u = to_f(in[r * 2 * I + I + j]);
-    out[t] = (T)(g / (1.0f + expf(-g)) * u);
+    const int64_t r = t / iv;
+    const int j = (int)(t - r * iv) * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(in + r * 2 * I + j);
+    const uint4 uv = *reinterpret_cast<const uint4*>(in + r * 2 * I + I + j);
+    const T* g = reinterpret_cast<const T*>(&gv);
+    const T* u = reinterpret_cast<const T*>(&uv);
+    uint4 ov;
+    T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float gf = to_f(g[i]);
+      o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(u[i]));
+    }
+    *reinterpret_cast<uint4*>(out + r * I + j) = ov;
   }
 }
 
-// out[m, h] = sum over k of in[m, k, h] (fp32 accumulate). With ids given,
-// only pairs whose expert lies in [e_begin, e_end) are summed.
+// out[m, h] = sum over k of in[m, k, h] (fp32 accumulate), eight features per
+// thread (H % 8 == 0). With ids given, only pairs whose expert lies in
+// [e_begin, e_end) are summed.
 template <typename T>
 __global__ void topk_sum_kernel(const T* __restrict__ in, int M, int topk, int H,
                                 const int32_t* __restrict__ ids, int e_begin, int e_end,
                                 T* __restrict__ out) {
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < (int64_t)M * H;
+  const int hv = H / 8;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < (int64_t)M * hv;
        t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = t / H;
-    const int h = (int)(t - m * H);
-    float acc = 0.f;
+    const int64_t m = t / hv;
+    const int h = (int)(t - m * hv) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int k = 0; k < topk; ++k) {
       if (ids != nullptr) {
         const int e = ids[m * topk + k];
         if (e < e_begin || e >= e_end) continue;
       }
-      acc += to_f(in[(m * topk + k) * H + h]);
+      const uint4 v = *reinterpret_cast<const uint4*>(in + (m * topk + k) * H + h);
+      const T* vt = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] += to_f(vt[i]);
     }
-    out[t] = (T)acc;
+    uint4 ov;
+    T* o = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = (T)acc[i];
+    *reinterpret_cast<uint4*>(out + m * H + h) = ov;
   }
 }
 
@@ -241,7 +288,7 @@ extern "C" int awqb_moe_align(const int32_t* topk_ids, int64_t numel, int64_t e_
                (long long)(numel + E * (block_m - 1)));
   AWQB_REQUIRE(sorted_ids && block_expert && num_post_pad && (numel == 0 || topk_ids),
                kInvalidArgument, "null pointer");
-  const size_t smem = (size_t)(32 * E + E + 1) * sizeof(int32_t);
+  const size_t smem = (size_t)(32 * E + E + 1 + 32) * sizeof(int32_t);
   auto kern = align_kernel;
   AWQB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   kern<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(
@@ -269,11 +316,14 @@ extern "C" int awqb_moe_gather_rows(const void* x, int64_t K, const int32_t* sor
 
 extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
                                  int dtype, void* out, void* stream) {
-  AWQB_REQUIRE(I > 0 && rows_max >= 0, kInvalidArgument, "bad sizes");
+  AWQB_REQUIRE(I > 0 && I % 8 == 0 && rows_max >= 0, kInvalidArgument, "I=%lld must be a positive multiple of 8",
+               (long long)I);
+  AWQB_REQUIRE(((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0, kInvalidArgument,
+               "in and out must be 16-byte aligned");
   AWQB_REQUIRE(in && out, kInvalidArgument, "null pointer");
   if (rows_max == 0) return kOk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned g = grid1d(rows_max * I, 256);
+  const unsigned g = grid1d(rows_max * (I / 8), 256);
   if (dtype == AWQB_DTYPE_F16)
     silu_and_mul_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(in), rows_max, rows_dev,
                                                    (int)I, static_cast<__half*>(out));
@@ -290,11 +340,13 @@ extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t
 extern "C" int awqb_moe_topk_sum(const void* in, int64_t M, int64_t topk, int64_t H,
                                  const int32_t* topk_ids, int64_t e_begin, int64_t e_end, int dtype,
                                  void* out, void* stream) {
-  AWQB_REQUIRE(M >= 0 && topk >= 1 && H >= 1, kInvalidArgument, "bad sizes");
+  AWQB_REQUIRE(M >= 0 && topk >= 1 && H >= 8 && H % 8 == 0, kInvalidArgument, "bad sizes (H % 8 != 0)");
   if (M == 0) return kOk;
   AWQB_REQUIRE(in && out, kInvalidArgument, "null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const unsigned g = grid1d(M * H, 256);
+  AWQB_REQUIRE(((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0, kInvalidArgument,
+               "in and out must be 16-byte aligned");
+  const unsigned g = grid1d(M * (H / 8), 256);
   if (dtype == AWQB_DTYPE_F16)
     topk_sum_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(in), (int)M, (int)topk, (int)H,
                                                topk_ids, (int)e_begin, (int)e_end,
