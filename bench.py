@@ -348,7 +348,10 @@ def run_ours(args):
                    "parallelism": f"tp{world}", "l2": "working set 453 MB > 126 MB L2, no flush"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
-                     "traffic": (traffic or {}).get("dram_bytes_per_step"),
+                     "traffic": (traffic["dram_bytes_per_step"] / traffic["launches_per_step"]
+                                 if traffic and world == 1 else None),
+                     "traffic_source": "profiles/gemm_decode_llama8b_traffic.json (ncu, mean per launch)",
+                     "algorithmic_bytes_per_launch": algo / len(order),
                      "algorithmic_bytes_per_step": algo,
                      "mean_gemm_us": gemm_ms * 1e3 / (args.steps * len(order))},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
@@ -458,6 +461,23 @@ def run_single(args):
                       "frac_hbm": b / us / 1e3 / hbm, "peak_kind": kind}), flush=True)
 
 
+def run_gemm(args):
+    """One projection, plain launches (no graph): the case the ncu captures profile."""
+    from sglite_b200 import ops
+
+    K, N, M = (int(v) for v in args.shape.split("x"))
+    dtype = torch.float16 if args.fp16 else DTYPE
+    dev = torch.device("cuda", 0)
+    _, w = _linear(K, N, dev, dtype, 0)
+    x = torch.randn((M, K), device=dev).to(dtype)
+    y = torch.empty((M, N), device=dev, dtype=dtype)
+    for _ in range(args.warmup + args.steps):
+        ops.gemm(x, w["qweight"], K, N, G, out=y)
+    torch.cuda.synchronize()
+    print(json.dumps({"workload": f"gemm K={K} N={N} M={M}", "launches": args.warmup + args.steps,
+                      "dtype": str(dtype), "device_error": ops.device_error()}), flush=True)
+
+
 def run_tp70b(args):
     """Config 3: Llama-3.1-70B layer projections under TP=N, all-reduce after O and down."""
     import torch.distributed as dist
@@ -556,8 +576,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe", "gemm"],
                     help="decode (default, the contract line) or another BASELINE config")
+    ap.add_argument("--shape", default="4096x28672x1", help="KxNxM for --workload gemm")
+    ap.add_argument("--fp16", action="store_true", help="fp16 activations for --workload gemm")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -571,6 +593,8 @@ def main():
         run_tp70b(args)
     elif args.workload == "moe":
         run_moe(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
     else:
         run_ours(args)
 

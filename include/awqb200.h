@@ -63,8 +63,11 @@ int awqb_dequant(const void* blob, int64_t batch, int64_t K, int64_t N, int64_t 
  * apply_awq_marlin_linear, marlin_utils.py:355-415.
  * x, y, bias are in the activation dtype; x 16-byte aligned, rows contiguous.
  * fp32 accumulation. The workspace (size from awqb_gemm_workspace_bytes) must
- * be 256-byte aligned and zero-filled before its first use; every call leaves
- * it zero-filled again. Calls that share a workspace must not overlap in time.
+ * be 256-byte aligned. Its first 8 KiB hold split-tile counters: zero them
+ * before the first use; every call leaves them zero again (the rest is scratch
+ * for fp32 partial tiles). Calls of any shape may share one workspace as long
+ * as it is large enough for each; calls that share it must not overlap in time.
+ * At most 1024 CTAs.
  */
 int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t G, int64_t* bytes);
 int awqb_gemm(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,

@@ -102,6 +102,10 @@ struct Plan {
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
 
+// At most kMaxCtas persistent CTAs; two int32 counters each.
+constexpr int kMaxCtas = 1024;
+constexpr int64_t kCounterBytes = 2 * 4 * kMaxCtas;
+
 bool valid_group(int64_t G) { return G == 32 || G == 64 || (G >= 128 && G % 128 == 0); }
 
 int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, Plan* pl) {
@@ -135,7 +139,10 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   if (c > U) c = U;
   if (c < 1) c = 1;
   pl->ctas = c;
-  pl->cnt_bytes = round_up((int64_t)pl->MT * pl->NT * 4, 256);
+  AWQB_REQUIRE(c <= kMaxCtas, kInvalidArgument, "ctas=%lld above the limit %d", (long long)c, kMaxCtas);
+  // Counters live in a fixed region at the start of every workspace, so calls
+  // with different plans sharing one workspace never write partials over them.
+  pl->cnt_bytes = kCounterBytes;
   pl->part_bytes = c * 2 * 128 * (int64_t)pl->ntok * 4;
   return kOk;
 }

@@ -29,10 +29,12 @@
 // Work partition (stream-K): the (tile, k-block) units of the whole problem are
 // split evenly over the persistent CTAs; a CTA walks its units as segments,
 // one per tile it touches. A tile covered by a single CTA is stored directly;
-// a tile shared by several CTAs is reduced by whichever contributor finishes
-// last (an atomic counter per tile; nobody waits), summing the partials in
-// contributor order so the result is deterministic. The accumulator is double
-// buffered in TMEM so the epilogue of one segment overlaps the next mainloop.
+// a tile shared by several CTAs is reduced by the contributor that arrives last
+// (an arrival ticket per tile): it keeps its own partial in TMEM and waits only
+// for peers that have already arrived to publish theirs, summing the partials
+// in contributor order so the result is deterministic. The accumulator is
+// double buffered in TMEM so the epilogue of one segment overlaps the next
+// mainloop.
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -77,7 +79,8 @@ struct GemmParams {
   int32_t M, N, K;
   int32_t NT, KB, MT;           // feature tiles, k-blocks, token tiles (max)
   float* ws_part;               // [gridDim.x][2][128 rows][NTOK] fp32 partial tiles
-  int32_t* ws_cnt;              // [MT * NT] arrival counters, zero between calls
+  int32_t* ws_cnt;              // [gridDim.x][2] arrived / published counters of the split tile
+                                //   each CTA owns; zero between calls
   uint32_t* err;                // device error word
   int32_t x3d;                  // X tensor map is 3-D {64, rows, K/64}: one load per stage
 };
@@ -110,7 +113,7 @@ struct GemmCfg {
   static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK + (kATmem ? kSD * kAStageCols : 0)));
   static_assert(kSD >= 2, "need two A stages");
   static_assert(kTmemCols <= 512, "TMEM over capacity");
-  static_assert((2 * kSL + 2 * kSD + 5) * 8 + 16 <= 512, "barrier area overflow");
+  static_assert((2 * kSL + 2 * kSD + 6) * 8 + 16 <= 512, "barrier area overflow");
   static_assert(kSL >= 2, "not enough shared memory for two load stages");
   static_assert(kSmemBytes <= 232448, "shared memory over the sm_100 per-CTA limit");
   static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "MMA N must be 16..256 step 16");
@@ -181,7 +184,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   uint64_t* acc_full = empty_d + SD;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
   uint64_t* drain = acc_empty + 2;     // [1]
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* red_bar = drain + 1;       // [1]  peers' partials landed (bulk-copy reduction)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(red_bar + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_flag = reinterpret_cast<volatile int*>(s_tmem + 2);  // [2]
 
@@ -217,6 +221,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       mbar_init(smem_u32(&acc_empty[i]), Cfg::kNumEpiWarps);
     }
     mbar_init(smem_u32(drain), 1);
+    mbar_init(smem_u32(red_bar), 1);
     *s_abort = 0;
     prefetch_tmap(&tmap_x);
     fence_barrier_init();
@@ -403,6 +408,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
     const int f = q * 32 + lane;            // feature row within the tile
     const int etid = threadIdx.x - Cfg::kEpiWarp0 * 32;
+    constexpr int kEpiThreads = Cfg::kNumEpiWarps * 32;
     grid_dep_wait();  // outputs, workspace counters and partials belong to the previous grid until then
     RingPos acc;
     for (int u = u_begin; u < u_end; acc.next<2>()) {
@@ -425,58 +431,67 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       // The owner holds the tile's first unit. The tile runs past its range, so
       // this is its last segment and the other TMEM accumulator buffer is free.
       const bool owner = split && c_first == (int)blockIdx.x;
+      // A split tile is the last segment of its first contributor, so each CTA
+      // owns at most one: the tile's counters are indexed by that contributor.
+      int32_t* const cnt = p.ws_cnt + 2 * c_first;
       const uint32_t lane_off = (uint32_t)(q * 32) << 16;
       const uint32_t t_addr = tmem_base + lane_off + (uint32_t)(acc.idx * NTOK);
       const uint32_t t_spare = tmem_base + lane_off + (uint32_t)((acc.idx ^ 1) * NTOK);
-      // Partial of contributor cj (slot 0 = its first segment, 1 = its last).
+      // Partial of contributor cj (slot 0 = its first segment, 1 = its last),
+      // column-major [NTOK][128]: column c of feature f at [c * 128 + f], so a
+      // warp moves 128 contiguous bytes per column.
       auto part_of = [&](int cj) -> const float* {
         const int64_t cb = (int64_t)cj * U / C;
         const int cs = (cb >= t_begin) ? 0 : 1;
-        return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK) + f * NTOK;
+        return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK);
       };
 
       // Wait for the accumulator. Meanwhile an owner whose peers have all
-      // published their partials sums them (in contributor order) into the spare
-      // TMEM buffer, so the fix-up costs nothing once its own MMAs are done.
+      // published sums their partials (in contributor order) into the spare TMEM
+      // buffer, so the fix-up costs nothing once its own MMAs are done; it gives
+      // up as soon as its accumulator is ready (the reducer path then runs).
       bool pre = false;
       {
         const uint32_t bar = smem_u32(&acc_full[acc.idx]);
         bool done = mbar_try_wait(bar, acc.phase);
+        bool tried = false;
         const uint64_t t0 = done ? 0 : globaltimer_ns();
         while (!done) {
-          if (owner && !pre) {
+          if (owner && !tried) {
             // every lane acquires for itself; the decision is warp-uniform
-            if (__all_sync(0xffffffffu, ld_acquire_gpu(&p.ws_cnt[tile]) == ncontrib - 1)) {
+            if (__all_sync(0xffffffffu, ld_acquire_gpu(&cnt[1]) == ncontrib - 1)) {
+              tried = true;
+              bool complete = true;
 #pragma unroll 1
-              for (int c0 = 0; c0 < rows_here; c0 += 16) {
-                const int nv = cmin(4, (rows_here - c0 + 3) >> 2);
-                float sum[16];
+              for (int c0 = 0; c0 < rows_here; c0 += 8) {
+                if (c0 > 0 && mbar_test_wait(bar, acc.phase)) {
+                  complete = false;
+                  done = true;
+                  break;
+                }
+                float sum[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) sum[i] = 0.f;
+                for (int i = 0; i < 8; ++i) sum[i] = 0.f;
 #pragma unroll 1
                 for (int cj = c_first + 1; cj <= c_last; ++cj) {
-                  const float4* src = reinterpret_cast<const float4*>(part_of(cj) + c0);
-                  float4 a[4];
+                  const float* src = part_of(cj) + c0 * 128 + f;
+                  float a[8];
 #pragma unroll
-                  for (int i = 0; i < 4; ++i) a[i] = (i < nv) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  for (int i = 0; i < 8; ++i) a[i] = (c0 + i < rows_here) ? __ldcg(src + i * 128) : 0.f;
 #pragma unroll
-                  for (int i = 0; i < 4; ++i) {
-                    sum[4 * i] += a[i].x;
-                    sum[4 * i + 1] += a[i].y;
-                    sum[4 * i + 2] += a[i].z;
-                    sum[4 * i + 3] += a[i].w;
-                  }
+                  for (int i = 0; i < 8; ++i) sum[i] += a[i];
                 }
-                uint32_t sv[16];
+                uint32_t sv[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) sv[i] = __float_as_uint(sum[i]);
-                tmem_st16(t_spare + (uint32_t)c0, sv);
+                for (int i = 0; i < 8; ++i) sv[i] = __float_as_uint(sum[i]);
+                tmem_st8(t_spare + (uint32_t)c0, sv);
               }
               tmem_st_wait();
-              pre = true;
+              pre = complete;
+              if (done) break;
             }
           }
-          done = mbar_try_wait_hint(bar, acc.phase, (owner && !pre) ? 1000u : 20000u);
+          done = mbar_try_wait_hint(bar, acc.phase, (owner && !tried) ? 1000u : 20000u);
           if (!done && globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) break;
         }
         if (!done) {
@@ -525,7 +540,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         }
       };
 
-      const bool fast = split && named_bar_and(1, Cfg::kNumEpiWarps * 32, owner && pre);
+      const bool fast = split && named_bar_and(1, kEpiThreads, owner && pre);
       if (!split || fast) {
         // Whole tile, or an owner with its peers' sum ready: final values now.
 #pragma unroll 1
@@ -549,74 +564,123 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
-        if (fast && etid == 0) p.ws_cnt[tile] = 0;  // every peer has arrived; nobody else touches it
+        if (fast && etid == 0) {  // every peer has published; nobody else touches the counters
+          cnt[0] = 0;
+          cnt[1] = 0;
+        }
       } else {
-        // Publish this CTA's partial: slot 0 holds its first segment, slot 1 its
-        // last. Row-major [128][NTOK] so each thread moves its row with 16-byte
-        // accesses.
-        const int slot = (u == u_begin) ? 0 : 1;
-        float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK) + f * NTOK;
-#pragma unroll 1
-        for (int c0 = 0; c0 < ncols; c0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(t_addr + c0, v);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c = 0; c < 16; c += 4)
-            if (c0 + c < rows_here)
-              __stcg(reinterpret_cast<float4*>(part + c0 + c),
-                     make_float4(__uint_as_float(v[c]), __uint_as_float(v[c + 1]),
-                                 __uint_as_float(v[c + 2]), __uint_as_float(v[c + 3])));
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
-        // Arrive on the tile counter: the block barrier orders every thread's
-        // partial stores before thread 0's release-ordered add (cumulativity).
-        named_bar_sync(1, Cfg::kNumEpiWarps * 32);
+        // Take an arrival ticket. The last contributor to arrive reduces the
+        // tile: it keeps its own partial in TMEM and waits for the others to
+        // publish theirs. Everyone else publishes. A reducer only ever waits for
+        // CTAs that have already arrived (so are running): no co-residency of
+        // the grid is assumed.
         if (etid == 0) {
-          const int prev = atom_add_release_gpu(&p.ws_cnt[tile], 1);
-          const int last = (prev == ncontrib - 1) ? 1 : 0;
-          if (last) {
-            fence_acquire_gpu();  // the other contributors' partials
-            p.ws_cnt[tile] = 0;
-          }
-          s_flag[acc.idx] = last;
+          const int prev = atom_add_relaxed_gpu(&cnt[0], 1);
+          s_flag[acc.idx] = (prev == ncontrib - 1) ? 1 : 0;
         }
-        named_bar_sync(1, Cfg::kNumEpiWarps * 32);
-        if (s_flag[acc.idx]) {
-          // Sum in the owner-last order (c_first+1 .. c_last, then c_first) so
-          // the result does not depend on which contributor finished last.
+        named_bar_sync(1, kEpiThreads);
+        const bool reducer = s_flag[acc.idx] != 0;
+        if (!reducer) {
+          // Publish: slot 0 holds this CTA's first segment, slot 1 its last.
+          const int slot = (u == u_begin) ? 0 : 1;
+          float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK) + f;
 #pragma unroll 1
-          for (int c0 = 0; c0 < rows_here; c0 += 8) {
-            const int nv = cmin(2, (rows_here - c0 + 3) >> 2);  // float4s holding live rows
-            float4 acc4[2];
-            acc4[0] = acc4[1] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-            for (int cb = 0; cb < ncontrib; cb += 4) {
-              float4 a[4][2];
+          for (int c0 = 0; c0 < ncols; c0 += 16) {
+            uint32_t v[16];
+            tmem_ld16(t_addr + c0, v);
+            tmem_ld_wait();
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int idx = cb + j;
-                const bool live = idx < ncontrib;
-                const int cj = (idx < ncontrib - 1) ? c_first + 1 + idx : c_first;
-                const float4* src = reinterpret_cast<const float4*>(part_of(cj) + c0);
-#pragma unroll
-                for (int i = 0; i < 2; ++i)
-                  a[j][i] = (live && i < nv) ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                  acc4[i].x += a[j][i].x;
-                  acc4[i].y += a[j][i].y;
-                  acc4[i].z += a[j][i].z;
-                  acc4[i].w += a[j][i].w;
-                }
-            }
-            store_row_vals(c0, reinterpret_cast<const float*>(acc4), 8);
+            for (int c = 0; c < 16; ++c)
+              if (c0 + c < rows_here) __stcg(part + (c0 + c) * 128, __uint_as_float(v[c]));
           }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
+          // The block barrier orders every thread's partial stores before thread
+          // 0's release-ordered add (cumulativity).
+          named_bar_sync(1, kEpiThreads);
+          if (etid == 0) red_add_release_gpu(&cnt[1], 1);
+        } else {
+          // Sequence order of the sum: c_first+1 .. c_last, then c_first. On the
+          // CTA's last segment the load ring is idle (every MMA has completed), so
+          // the peers' partials come in with one bulk copy each; otherwise they
+          // are loaded into registers.
+          const int me = (int)blockIdx.x;
+          const int s_me = (me == c_first) ? ncontrib - 1 : me - c_first - 1;
+          const int peer_bytes = rows_here * 128 * 4;
+          const bool bulk = seg_end == u_end && (int64_t)(ncontrib - 1) * peer_bytes <= (int64_t)SL * Cfg::kLStage;
+          if (etid == 0) {
+            // Bounded wait for the other ncontrib - 1 partials.
+            int ok = 1;
+            if (ld_acquire_gpu(&cnt[1]) != ncontrib - 1) {
+              const uint64_t t0 = globaltimer_ns();
+              while (ld_acquire_gpu(&cnt[1]) != ncontrib - 1) {
+                if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+                  atomicOr(p.err, kErrWaitEpilogue);
+                  ok = 0;
+                  break;
+                }
+              }
+            }
+            if (ok) {
+              cnt[0] = 0;
+              cnt[1] = 0;
+              if (bulk && peer_bytes > 0) {
+                fence_proxy_async_global();  // peers' generic stores -> bulk-copy reads
+                const uint32_t rb = smem_u32(red_bar);
+                mbar_arrive_expect_tx(rb, (uint32_t)((ncontrib - 1) * peer_bytes));
+                for (int s = 0; s < ncontrib; ++s) {
+                  if (s == s_me) continue;
+                  const int cj = (s < ncontrib - 1) ? c_first + 1 + s : c_first;
+                  const int slot = s < s_me ? s : s - 1;
+                  bulk_g2s(smem_u32(lring + (size_t)slot * peer_bytes), part_of(cj), (uint32_t)peer_bytes, rb,
+                           policy_evict_first());
+                }
+              }
+            }
+            s_flag[acc.idx] = ok ? 1 : 2;
+          }
+          named_bar_sync(1, kEpiThreads);
+          if (s_flag[acc.idx] == 1) {
+            bool have = true;
+            if (bulk && peer_bytes > 0) {
+              have = mbar_wait(smem_u32(red_bar), 0);
+              if (!have && etid == 0) atomicOr(p.err, kErrWaitEpilogue);
+            }
+            const float* sm = reinterpret_cast<const float*>(lring) + f;
+#pragma unroll 1
+            for (int c0 = 0; have && c0 < rows_here; c0 += 8) {
+              uint32_t ov[8];
+              tmem_ld8(t_addr + c0, ov);
+              tmem_ld_wait();
+              float sum[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) sum[i] = 0.f;
+#pragma unroll 1
+              for (int s = 0; s < ncontrib; ++s) {
+                float a[8];
+                if (s == s_me) {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) a[i] = __uint_as_float(ov[i]);
+                } else if (bulk) {
+                  const float* src = sm + (size_t)(s < s_me ? s : s - 1) * (peer_bytes / 4) + c0 * 128;
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) a[i] = (c0 + i < rows_here) ? src[i * 128] : 0.f;
+                } else {
+                  const int cj = (s < ncontrib - 1) ? c_first + 1 + s : c_first;
+                  const float* src = part_of(cj) + c0 * 128 + f;
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) a[i] = (c0 + i < rows_here) ? __ldcg(src + i * 128) : 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < 8; ++i) sum[i] += a[i];
+              }
+              store_row_vals(c0, sum, 8);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
         }
       }
       u = seg_end;

@@ -126,8 +126,9 @@ def dequant(blob: torch.Tensor, K: int, N: int, G: int, dtype: torch.dtype) -> t
 class _WorkspacePool:
     """One zero-filled scratch buffer per device, grown on demand.
 
-    The GEMM leaves its counters at zero after every call, so the buffer is
-    zeroed only when it is (re)allocated. Growing is refused while a CUDA graph
+    The GEMM keeps its split-tile counters in the first 8 KiB of any workspace
+    and leaves them at zero after every call, so the buffer is zeroed only when
+    it is (re)allocated; the rest is scratch shared by calls of every shape. Growing is refused while a CUDA graph
     is being captured: size it first (``reserve``) with the largest call.
     """
 

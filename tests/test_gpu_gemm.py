@@ -117,3 +117,22 @@ def test_gemm_full_size_linearity(cuda, name, K, N, M):
     Wsl = dequant_ref(w["qweight"][:, (N - 256) // 8:], w["qzeros"][:, (N - 256) // 8:], w["scales"][:, cols], G)
     ref = gemm_ref(x, Wsl)
     assert rel_err(ya[:, cols], ref) <= TOL
+
+
+def test_shared_workspace_mixed_shapes(cuda):
+    """Calls of different shapes and token tiles share the per-device workspace:
+    each result equals the one computed with a fresh zero-filled workspace (the
+    split-tile reduction order is fixed, so equality is exact)."""
+    G = 128
+    dtype = torch.bfloat16
+    shapes = [(4096, 4096), (4096, 6144), (2048, 7168), (7168, 1024)]
+    setups = [_setup(cuda, 1, K, N, G, dtype, seed=K + N) for K, N in shapes]
+    for rep in range(2):
+        for (K, N), (w, _, blob) in zip(shapes, setups):
+            for M in (1, 40, 300):
+                x = make_activations(M, K, dtype, seed=M + rep).to(cuda)
+                y_shared = ops.gemm(x, blob, K, N, G)
+                fresh = torch.zeros(ops.gemm_workspace_bytes(M, K, N, G), dtype=torch.uint8, device=cuda)
+                y_fresh = ops.gemm(x, blob, K, N, G, workspace=fresh)
+                assert torch.equal(y_shared, y_fresh), (K, N, M, rep)
+    assert ops.device_error() == 0
