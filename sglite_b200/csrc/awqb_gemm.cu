@@ -82,11 +82,14 @@ int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, i
 // in TMEM, 256-k stages) up to a few thousand tokens, where it keeps more tiles
 // in flight than SMs; 256 (weights in shared memory, each dequantised weight
 // reused by twice as many tokens) for the largest prefill batches.
+// Measured on B200 over the Llama-3 / Qwen3 projection shapes: 64-token tiles
+// (four load stages) beat 128-token tiles (two stages) up to about M = 1024;
+// 256-token tiles only pay above M = 4096.
 int choose_ntok(int64_t M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
-  if (M <= 64) return 64;
-  if (M <= 3072) return 128;
+  if (M <= 1024) return 64;
+  if (M <= 4096) return 128;
   return 256;
 }
 
@@ -140,6 +143,10 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   if (c < 1) c = 1;
   pl->ctas = c;
   AWQB_REQUIRE(c <= kMaxCtas, kInvalidArgument, "ctas=%lld above the limit %d", (long long)c, kMaxCtas);
+  // The kernel's stream-K arithmetic is 32-bit: its unit indices times the CTA
+  // count stay below 2 C^2 (stages per tile).
+  AWQB_REQUIRE(2 * c * c * (pl->KB / stage_blocks(pl->ntok)) < (1ll << 31), kUnsupported,
+               "K=%lld too large for %lld CTAs", (long long)K, (long long)c);
   // Counters live in a fixed region at the start of every workspace, so calls
   // with different plans sharing one workspace never write partials over them.
   pl->cnt_bytes = kCounterBytes;
@@ -400,6 +407,8 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   if (rows_max == 0) return kOk;
   pl.ctas = grouped_ctas(0);
   pl.part_bytes = pl.ctas * 2 * 128 * (int64_t)pl.ntok * 4;
+  AWQB_REQUIRE(2 * pl.ctas * pl.ctas * (pl.KB / stage_blocks(pl.ntok)) < (1ll << 31), kUnsupported,
+               "K=%lld too large for %lld CTAs", (long long)K, (long long)pl.ctas);
   AWQB_REQUIRE(x_sorted && blobs && block_expert && num_post_pad && y, kInvalidArgument, "null pointer");
   AWQB_REQUIRE(((uintptr_t)x_sorted & 15) == 0 && ((uintptr_t)blobs & 15) == 0 && blob_stride % 16 == 0,
                kInvalidArgument, "x_sorted, blobs and blob_stride must be 16-byte aligned");

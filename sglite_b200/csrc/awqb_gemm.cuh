@@ -26,9 +26,11 @@
 //                 the write + MMA read of a smem copy would cost 4 bytes of
 //                 shared-memory bandwidth per weight.
 //
-// Work partition (stream-K): the (tile, k-block) units of the whole problem are
-// split evenly over the persistent CTAs; a CTA walks its units as segments,
-// one per tile it touches. A tile covered by a single CTA is stored directly;
+// Work partition (Sched): persistent CTAs take whole tiles round-robin while at
+// least two full waves remain (neighbouring CTAs share activations in L2), then
+// the (tile, stage) units of the last waves are split evenly over the CTAs
+// (stream-K); a CTA walks its units as segments, one per tile it touches. A
+// tile covered by a single CTA is stored directly;
 // a tile shared by several CTAs is reduced by the contributor that arrives last
 // (an arrival ticket per tile): it keeps its own partial in TMEM and waits only
 // for peers that have already arrived to publish theirs, summing the partials
@@ -120,11 +122,6 @@ struct GemmCfg {
   static_assert(kPkBytes % 16 == 0, "bulk copy size must be a multiple of 16");
 };
 
-// Owner of unit u when U units are split over C CTAs as [cU/C, (c+1)U/C).
-__device__ __forceinline__ int unit_owner(int u, int U, int C) {
-  return (int)((((int64_t)u + 1) * C - 1) / U);
-}
-
 // Ring slot + phase bit, advanced without divisions.
 struct RingPos {
   int idx = 0;
@@ -138,23 +135,106 @@ struct RingPos {
   }
 };
 
-// Walks (tile, stage) units in order: stage kb fastest, then feature tile nt,
-// then token tile mt.
-struct UnitPos {
-  int u, kb, nt, mt;
-  __device__ __forceinline__ void init(int u0, int KBS, int NT) {
-    u = u0;
-    const int tile = u0 / KBS;
-    kb = u0 - tile * KBS;
-    mt = tile / NT;
-    nt = tile - mt * NT;
+// Work of one CTA, as a sequence of "local" units j = 0 .. n_local-1 (a unit is
+// one pipeline stage of one tile; tiles are numbered t = mt * NT + nt).
+//  * Data-parallel phase, while at least two full waves of tiles remain: whole
+//    tiles c, c + C, c + 2C, ... Concurrent CTAs work on neighbouring tiles, so
+//    they share activation rows (and weights) in L2.
+//  * Stream-K phase over the units of the last one to two waves, split evenly
+//    into contiguous ranges [c U_sk / C, (c+1) U_sk / C). Tiles cut by a range
+//    boundary are reduced across their contributors (see the epilogue).
+// Decode-sized problems (fewer tiles than two waves) are stream-K only.
+struct Sched {
+  int KBS, NT, C, c;
+  int C_mt, C_nt;  // C = C_mt * NT + C_nt: the tile step of the data-parallel phase
+  int dp_units;  // units of this CTA's data-parallel tiles
+  int sk_base;   // first global unit of the stream-K phase (a tile boundary)
+  int U_sk;      // units in the stream-K phase (>= C)
+  int sk_begin;  // this CTA's stream-K range start, relative to sk_base
+  int n_local;   // units this CTA processes (0 for CTAs >= C)
+  __device__ __forceinline__ void init(int T, int KBS_, int NT_, int grid, int cta) {
+    KBS = KBS_;
+    NT = NT_;
+    const int U = T * KBS;
+    C = grid < U ? grid : U;  // never more CTAs than units: each CTA below C has work
+    c = cta;
+    C_mt = C / NT;
+    C_nt = C - C_mt * NT;
+    const int waves = T / C;
+    const int n_dp = waves >= 2 ? waves - 1 : 0;
+    dp_units = n_dp * KBS;
+    sk_base = n_dp * C * KBS;
+    U_sk = U - sk_base;
+    if (cta >= C) {
+      dp_units = 0;
+      sk_begin = 0;
+      n_local = 0;
+      return;
+    }
+    sk_begin = sk_start(cta);
+    n_local = dp_units + sk_start(cta + 1) - sk_begin;
   }
-  __device__ __forceinline__ void next(int KBS, int NT) {
-    ++u;
-    if (++kb == KBS) {
+  // Stream-K: first unit (relative) of contributor cj, and the owner of unit r.
+  // U_sk < 2 C KBS, so the products stay below 2 C^2 KBS < 2^31 (checked by
+  // the host) and 32-bit unsigned arithmetic suffices.
+  __device__ __forceinline__ int sk_start(int cj) const { return (int)((unsigned)cj * (unsigned)U_sk / (unsigned)C); }
+  __device__ __forceinline__ int sk_owner(int r) const {
+    return (int)(((unsigned)r * (unsigned)C + (unsigned)C - 1u) / (unsigned)U_sk);
+  }
+  // Global unit of local unit j in the stream-K phase.
+  __device__ __forceinline__ int sk_global(int j) const { return sk_base + sk_begin + (j - dp_units); }
+  __device__ __forceinline__ int tile_of(int j) const {
+    return j < dp_units ? c + (j / KBS) * C : sk_global(j) / KBS;
+  }
+  // End (exclusive, local) of the segment - the run of units of one tile - holding j.
+  __device__ __forceinline__ int seg_end(int j) const {
+    if (j < dp_units) return (j / KBS + 1) * KBS;
+    const int g = sk_global(j);
+    const int e = j + ((g / KBS + 1) * KBS - g);
+    return e < n_local ? e : n_local;
+  }
+};
+
+// Walks a CTA's local units: stage kb, tile and its (mt, nt), without
+// divisions after init.
+struct WorkPos {
+  int j, kb, tile, nt, mt;
+  __device__ __forceinline__ void set_tile(int t, const Sched& s) {
+    tile = t;
+    mt = t / s.NT;
+    nt = t - mt * s.NT;
+  }
+  __device__ __forceinline__ void init(int j0, const Sched& s) {
+    j = j0;
+    if (j0 < s.dp_units) {
+      const int w = j0 / s.KBS;
+      kb = j0 - w * s.KBS;
+      set_tile(s.c + w * s.C, s);
+    } else {
+      const int g = s.sk_global(j0);
+      const int t = g / s.KBS;
+      kb = g - t * s.KBS;
+      set_tile(t, s);
+    }
+  }
+  __device__ __forceinline__ void next(const Sched& s) {
+    ++j;
+    if (j == s.dp_units) {  // into the stream-K range, which may start mid-tile
+      init(j, s);
+      return;
+    }
+    if (++kb == s.KBS) {
       kb = 0;
-      if (++nt == NT) {
-        nt = 0;
+      if (j < s.dp_units) {  // next data-parallel tile: tile + C
+        tile += s.C;
+        nt += s.C_nt;
+        mt += s.C_mt;
+      } else {
+        ++tile;
+        ++nt;
+      }
+      if (nt >= s.NT) {
+        nt -= s.NT;
         ++mt;
       }
     }
@@ -192,7 +272,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- work partition (identical in every role; all 32-bit, U < 2^31)
+  // ---- work partition (identical in every role; all 32-bit, units < 2^31)
   int MT = p.MT;
   if (p.rows_valid != nullptr) {
     const int rows = *p.rows_valid;
@@ -200,12 +280,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   }
   const int KB = p.KB, NT = p.NT;
   const int KBS = KB / SB;  // stages per tile (KB is even)
-  const int U = MT * NT * KBS;
-  // Never more contributors than units, so every CTA below C owns >= 1 unit.
-  const int C = (int)gridDim.x < U ? (int)gridDim.x : U;
-  const bool has_work = (int)blockIdx.x < C;
-  const int u_begin = has_work ? (int)((int64_t)blockIdx.x * U / C) : 0;
-  const int u_end = has_work ? (int)((int64_t)(blockIdx.x + 1) * U / C) : 0;
+  Sched sch;
+  sch.init(MT * NT, KBS, NT, (int)gridDim.x, (int)blockIdx.x);
+  const int n_local = sch.n_local;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SL; ++i) {
@@ -251,7 +328,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   }
   const uint32_t tmem_a_base = tmem_base + (uint32_t)Cfg::kAcol0;
 
-  if (!has_work || u_begin >= u_end) {
+  if (n_local == 0) {
     // nothing to do for this CTA
   } else if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -260,18 +337,18 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     const uint64_t pol_w = policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     RingPos st;
-    UnitPos up;
-    up.init(u_begin, KBS, NT);
+    WorkPos up;
+    up.init(0, sch);
     int issued = 0;
     const uint8_t* blob = p.blob;
     int blob_mt = -1;
     // Weights do not depend on the previous kernel in the stream: the first
     // stages' weight copies go out before waiting for it, their activations
     // after (each stage's barrier expects both).
-    const int early = cmin(SL, u_end - u_begin);
+    const int early = cmin(SL, n_local);
     {
-      UnitPos ue = up;
-      for (int j = 0; j < early; ++j, ue.next(KBS, NT)) {
+      WorkPos ue = up;
+      for (int j = 0; j < early; ++j, ue.next(sch)) {
         if (p.tile_expert != nullptr) {
           // expert ids are written by the routing kernel: wait before reading them
           break;
@@ -287,7 +364,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     }
     const bool weights_early = (p.tile_expert == nullptr);
     grid_dep_wait();
-    for (; up.u < u_end; up.next(KBS, NT)) {
+    for (; up.j < n_local; up.next(sch)) {
       if (issued >= SL) {
         if (!mbar_wait(smem_u32(&empty_l[st.idx]), st.phase ^ 1u)) {
           if (lane == 0) atomicOr(p.err, kErrWaitProducer);
@@ -344,9 +421,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     RingPos sl, sd, acc;
     int seg = 0;
     bool ok = true;
-    for (int u = u_begin; u < u_end && ok; ++seg) {
-      const int tile = u / KBS;
-      const int seg_end = cmin((tile + 1) * KBS, u_end);
+    for (int u = 0; u < n_local && ok; ++seg) {
+      const int seg_end = sch.seg_end(u);
       const int seg_begin = u;
       if (seg >= 2) {
         if (!mbar_wait(smem_u32(&acc_empty[acc.idx]), acc.phase ^ 1u)) {
@@ -411,11 +487,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     constexpr int kEpiThreads = Cfg::kNumEpiWarps * 32;
     grid_dep_wait();  // outputs, workspace counters and partials belong to the previous grid until then
     RingPos acc;
-    for (int u = u_begin; u < u_end; acc.next<2>()) {
-      const int tile = u / KBS;
-      const int t_begin = tile * KBS;
-      const int t_end = t_begin + KBS;
-      const int seg_end = cmin(t_end, u_end);
+    for (int u = 0; u < n_local; acc.next<2>()) {
+      const int tile = sch.tile_of(u);
+      const int seg_end = sch.seg_end(u);
       const int mt = tile / NT;
       const int nt = tile - mt * NT;
       const int n = nt * kBlockN + f;
@@ -424,8 +498,12 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       rows_here = cmax(0, cmin(NTOK, rows_here));
       const int ncols = (rows_here + 15) & ~15;
 
-      const int c_first = unit_owner(t_begin, U, C);
-      const int c_last = unit_owner(t_end - 1, U, C);
+      // Contributors: stream-K tiles may be cut by range boundaries; the
+      // data-parallel tiles are whole.
+      const bool sk = u >= sch.dp_units;
+      const int r_tile = tile * KBS - sch.sk_base;  // tile start relative to the stream-K phase
+      const int c_first = sk ? sch.sk_owner(r_tile) : (int)blockIdx.x;
+      const int c_last = sk ? sch.sk_owner(r_tile + KBS - 1) : (int)blockIdx.x;
       const int ncontrib = c_last - c_first + 1;
       const bool split = ncontrib > 1;
       // The owner holds the tile's first unit. The tile runs past its range, so
@@ -441,8 +519,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       // column-major [NTOK][128]: column c of feature f at [c * 128 + f], so a
       // warp moves 128 contiguous bytes per column.
       auto part_of = [&](int cj) -> const float* {
-        const int64_t cb = (int64_t)cj * U / C;
-        const int cs = (cb >= t_begin) ? 0 : 1;
+        const int cs = (sch.sk_start(cj) >= r_tile) ? 0 : 1;
         return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK);
       };
 
@@ -582,7 +659,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         const bool reducer = s_flag[acc.idx] != 0;
         if (!reducer) {
           // Publish: slot 0 holds this CTA's first segment, slot 1 its last.
-          const int slot = (u == u_begin) ? 0 : 1;
+          const int slot = (u == sch.dp_units) ? 0 : 1;  // first stream-K segment?
           float* part = p.ws_part + ((int64_t)blockIdx.x * 2 + slot) * (128 * NTOK) + f;
 #pragma unroll 1
           for (int c0 = 0; c0 < ncols; c0 += 16) {
@@ -608,7 +685,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
           const int me = (int)blockIdx.x;
           const int s_me = (me == c_first) ? ncontrib - 1 : me - c_first - 1;
           const int peer_bytes = rows_here * 128 * 4;
-          const bool bulk = seg_end == u_end && (int64_t)(ncontrib - 1) * peer_bytes <= (int64_t)SL * Cfg::kLStage;
+          const bool bulk = seg_end == n_local && (int64_t)(ncontrib - 1) * peer_bytes <= (int64_t)SL * Cfg::kLStage;
           if (etid == 0) {
             // Bounded wait for the other ncontrib - 1 partials.
             int ok = 1;
@@ -704,13 +781,13 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     const uint32_t st_off = (uint32_t)(h * 16384 + r * 128);
     int il = dg % SL, pl = (dg >= SL);    // load-ring slot / phase of this group's current stage
     int id = dg % SD, pd = (dg >= SD);    // A-ring slot / phase
-    for (int u = u_begin + dg; u < u_end; u += 2) {
+    for (int u = dg; u < n_local; u += 2) {
       if (!mbar_wait(smem_u32(&full_l[il]), (uint32_t)pl)) {
         atomicOr(p.err, kErrWaitDequant);
         *s_abort = 1;
         break;
       }
-      if (u - u_begin >= SD) {
+      if (u >= SD) {
         if (!mbar_wait(smem_u32(&empty_d[id]), (uint32_t)pd ^ 1u)) {
           atomicOr(p.err, kErrWaitDequant);
           *s_abort = 1;

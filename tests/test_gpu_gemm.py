@@ -136,3 +136,15 @@ def test_shared_workspace_mixed_shapes(cuda):
                 y_fresh = ops.gemm(x, blob, K, N, G, workspace=fresh)
                 assert torch.equal(y_shared, y_fresh), (K, N, M, rep)
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("ntok", [64, 128, 256])
+def test_gemm_data_parallel_waves(cuda, ntok):
+    """Enough tiles for several waves: whole tiles are processed data-parallel
+    and only the last waves are split stream-K; checked against the oracle."""
+    M, K, N, G = 2304, 512, 4096, 128
+    w, x, blob = _setup(cuda, M, K, N, G, torch.float16, seed=ntok)
+    y = ops.gemm(x.to(cuda), blob, K, N, G, ntok=ntok)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y, ref) <= TOL
+    assert ops.device_error() == 0
