@@ -147,22 +147,30 @@ def cpu_baseline(sample_seconds: float = 15.0):
     done_bytes = 0
     t_total = 0.0
     order = [(n, M) for M in MS for n in SHAPES]
+    weights = {}
+    for j, (name, (K, N)) in enumerate(SHAPES.items()):
+        g = torch.Generator().manual_seed(j)
+        weights[name] = (torch.randint(-2**31, 2**31 - 1, (K, N // 8), generator=g, dtype=torch.int64).to(torch.int32),
+                         torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), generator=g, dtype=torch.int64).to(torch.int32),
+                         (torch.rand((K // G, N), generator=g) * 9e-3 + 1e-3).to(DTYPE))
     i = 0
-    while t_total < sample_seconds and i < 4 * len(order):
+    while t_total < sample_seconds and i < 64 * len(order):
         name, M = order[i % len(order)]
         K, N = SHAPES[name]
-        g = torch.Generator().manual_seed(i)
-        qw = torch.randint(-2**31, 2**31 - 1, (K, N // 8), generator=g, dtype=torch.int64).to(torch.int32)
-        qz = torch.randint(-2**31, 2**31 - 1, (K // G, N // 8), generator=g, dtype=torch.int64).to(torch.int32)
-        sc = (torch.rand((K // G, N), generator=g) * 9e-3 + 1e-3).to(DTYPE)
-        x = torch.randn((M, K), generator=g).to(DTYPE)
+        x = torch.randn((M, K), generator=torch.Generator().manual_seed(i)).to(DTYPE)
         t0 = time.perf_counter()
-        cpu_awq_linear(x, qw, qz, sc, G, compute_dtype=torch.float32)
+        cpu_awq_linear(x, *weights[name], G, compute_dtype=torch.float32)
         t_total += time.perf_counter() - t0
         done_bytes += awq_bytes(K, N)
         i += 1
     return {"value": done_bytes / t_total / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"{i} of the step's 16 projection GEMMs, dequantise + fp32 matmul per call, {t_total:.1f} s"}
+
+
+def bench_config(world: int) -> dict:
+    return {"workload": "llama3_8b_awq_decode_projections", "group_size": G,
+            "batch_sizes": list(MS), "projections": {k: list(v) for k, v in SHAPES.items()},
+            "parallelism": f"tp{world}", "l2": "working set 453 MB > 126 MB L2, no flush"}
 
 
 def run_reference(args):
@@ -195,7 +203,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": dt / steps * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "llama3_8b_awq_decode_projections", "sample": "O projection at M=1,8,32,64 per step"},
+        "config": dict(bench_config(world), sample="O projection at M=1,8,32,64 per step"),
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": "O projection (K=N=4096) at M=1,8,32,64 per step, dequantise + fp32 matmul"},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -343,9 +351,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded random AWQ weights and N(0,1) activations)",
-        "config": {"workload": "llama3_8b_awq_decode_projections", "group_size": G,
-                   "batch_sizes": list(MS), "projections": {k: list(v) for k, v in SHAPES.items()},
-                   "parallelism": f"tp{world}", "l2": "working set 453 MB > 126 MB L2, no flush"},
+        "config": bench_config(world),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": peak_kind,
                      "traffic": (traffic["dram_bytes_per_step"] / traffic["launches_per_step"]

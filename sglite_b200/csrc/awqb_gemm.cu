@@ -83,18 +83,18 @@ int make_x_tensor_map(CUtensorMap* tm, const void* x, int64_t rows, int64_t K, i
 // in flight than SMs; 256 (weights in shared memory, each dequantised weight
 // reused by twice as many tokens) for the largest prefill batches.
 // Measured on B200 over the Llama-3 / Qwen3 projection shapes: 64-token tiles
-// (four load stages) beat 128-token tiles (two stages) up to about M = 1024;
-// 256-token tiles only pay above M = 4096.
+// win up to about M = 1024, 128-token tiles (five 128-k load stages) above;
+// the 256-token tile (operand A in shared memory, two load stages) never wins
+// and is only built for explicit requests.
 int choose_ntok(int64_t M) {
   if (M <= 16) return 16;
   if (M <= 32) return 32;
   if (M <= 1024) return 64;
-  if (M <= 4096) return 128;
-  return 256;
+  return 128;
 }
 
 // 128-k blocks per pipeline stage of the kernel built for this token tile.
-int stage_blocks(int ntok) { return ntok <= 128 ? 2 : 1; }
+int stage_blocks(int ntok) { return ntok <= 64 ? 2 : 1; }  // must match GemmCfg::kSB
 
 struct Plan {
   int ntok, gpb;

@@ -8,7 +8,7 @@
 // Tile: 128 output features (MMA M, operand A = dequantised weights, K-major)
 //       x NTOK tokens (MMA N, operand B = activations, K-major), fp32
 //       accumulator in TMEM. One pipeline stage is kSB blocks of 128 input
-//       features: 256 for token tiles <= 128, 128 for the 256-token tile.
+//       features: 256 for token tiles <= 64, 128 for larger token tiles.
 //
 // Warp roles (22 warps):
 //   warp 0        producer: one bulk copy of the stage's packed weight blocks
@@ -96,7 +96,10 @@ struct GemmCfg {
   static constexpr int kDqGroupWarps = 8;
   static constexpr int kThreads = 32 * (kDqWarp0 + kNumDqWarps);
   static constexpr bool kATmem = NTOK <= 128;         // operand A (weights) in tensor memory
-  static constexpr int kSB = kATmem ? 2 : 1;           // 128-k blocks per pipeline stage
+  // 128-k blocks per pipeline stage: 256 k for small token tiles (fewer
+  // barrier round trips per weight byte), 128 k above so that five stages of
+  // activations fit in shared memory.
+  static constexpr int kSB = NTOK <= 64 ? 2 : 1;
   static constexpr int kDqPerStage = 8;                 // one group of warps dequantises a stage
   static constexpr int kPkBytes = block_bytes_for_gpb(GPB);   // one packed block
   static constexpr int kPkStage = kSB * kPkBytes;             // bytes of one stage's bulk copy
@@ -334,7 +337,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     // ------------------------------------------------------------ producer
     // The whole warp runs the loop (so addresses stay warp-uniform and live in
     // uniform registers); one elected lane issues the copies.
-    const uint64_t pol_w = policy_evict_first();
+    // Weights are read once per token tile: stream them past L2 when there is
+    // a single token tile (decode), keep them when later token tiles reuse them.
+    const uint64_t pol_w = MT > 1 ? policy_evict_normal() : policy_evict_first();
     const uint64_t pol_x = policy_evict_last();
     RingPos st;
     WorkPos up;
