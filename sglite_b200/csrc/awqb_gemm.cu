@@ -93,6 +93,16 @@ int choose_ntok(int64_t M) {
   return 128;
 }
 
+// Token tiles per raster group. Weights that fit comfortably in the 126 MB L2
+// are re-read from L2 by every token tile, and walking all feature tiles of
+// one token tile first maximises activation sharing; larger weights (and MoE
+// experts, whose token tiles differ in expert) are shared by groups of 8 token
+// tiles so that each weight tile is read from DRAM about once per group.
+int raster_group_m(int64_t K, int64_t N, bool grouped) {
+  const int64_t weight_bytes = K * N / 2;
+  return (grouped || weight_bytes > (40ll << 20)) ? 8 : 1;
+}
+
 // 128-k blocks per pipeline stage of the kernel built for this token tile.
 int stage_blocks(int ntok) { return ntok <= 64 ? 2 : 1; }  // must match GemmCfg::kSB
 
@@ -248,6 +258,7 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
   p.err = err;
   p.x3d = is3d;
+  p.group_m = raster_group_m(K, N, p.tile_expert != nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, true, s);
@@ -444,6 +455,7 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   p.ws_part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + pl.cnt_bytes);
   p.err = err;
   p.x3d = is3d;
+  p.group_m = raster_group_m(K, N, p.tile_expert != nullptr);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, false, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, false, s);

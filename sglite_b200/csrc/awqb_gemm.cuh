@@ -85,6 +85,7 @@ struct GemmParams {
                                 //   each CTA owns; zero between calls
   uint32_t* err;                // device error word
   int32_t x3d;                  // X tensor map is 3-D {64, rows, K/64}: one load per stage
+  int32_t group_m;              // token tiles per raster group (>= 1)
 };
 
 template <int NTOK, int GPB>
@@ -139,7 +140,7 @@ struct RingPos {
 };
 
 // Work of one CTA, as a sequence of "local" units j = 0 .. n_local-1 (a unit is
-// one pipeline stage of one tile; tiles are numbered t = mt * NT + nt).
+// one pipeline stage of one tile; tile t maps to (mt, nt) by tile_mn).
 //  * Data-parallel phase, while at least two full waves of tiles remain: whole
 //    tiles c, c + C, c + 2C, ... Concurrent CTAs work on neighbouring tiles, so
 //    they share activation rows (and weights) in L2.
@@ -148,21 +149,22 @@ struct RingPos {
 //    boundary are reduced across their contributors (see the epilogue).
 // Decode-sized problems (fewer tiles than two waves) are stream-K only.
 struct Sched {
-  int KBS, NT, C, c;
-  int C_mt, C_nt;  // C = C_mt * NT + C_nt: the tile step of the data-parallel phase
+  int KBS, NT, MT, C, c;
+  int GM;        // token tiles per raster group
   int dp_units;  // units of this CTA's data-parallel tiles
   int sk_base;   // first global unit of the stream-K phase (a tile boundary)
   int U_sk;      // units in the stream-K phase (>= C)
   int sk_begin;  // this CTA's stream-K range start, relative to sk_base
   int n_local;   // units this CTA processes (0 for CTAs >= C)
-  __device__ __forceinline__ void init(int T, int KBS_, int NT_, int grid, int cta) {
+  __device__ __forceinline__ void init(int MT_, int KBS_, int NT_, int GM_, int grid, int cta) {
     KBS = KBS_;
     NT = NT_;
+    MT = MT_;
+    GM = GM_ > 0 ? GM_ : 1;
+    const int T = MT * NT;
     const int U = T * KBS;
     C = grid < U ? grid : U;  // never more CTAs than units: each CTA below C has work
     c = cta;
-    C_mt = C / NT;
-    C_nt = C - C_mt * NT;
     const int waves = T / C;
     const int n_dp = waves >= 2 ? waves - 1 : 0;
     dp_units = n_dp * KBS;
@@ -186,6 +188,19 @@ struct Sched {
   }
   // Global unit of local unit j in the stream-K phase.
   __device__ __forceinline__ int sk_global(int j) const { return sk_base + sk_begin + (j - dp_units); }
+  // Raster: tiles run through groups of GM token tiles; inside a group the
+  // token tile varies fastest, so concurrent CTAs share feature tiles (weights
+  // read from DRAM once for up to GM token tiles) and a narrow band of
+  // activation rows. GM = 1 walks all feature tiles of one token tile first.
+  __device__ __forceinline__ void tile_mn(int t, int& mt, int& nt) const {
+    const int gsz = GM * NT;
+    const int g = t / gsz;
+    const int w = t - g * gsz;
+    const int m0 = g * GM;
+    const int gm = MT - m0 < GM ? MT - m0 : GM;
+    nt = w / gm;
+    mt = m0 + (w - nt * gm);
+  }
   __device__ __forceinline__ int tile_of(int j) const {
     return j < dp_units ? c + (j / KBS) * C : sk_global(j) / KBS;
   }
@@ -198,14 +213,13 @@ struct Sched {
   }
 };
 
-// Walks a CTA's local units: stage kb, tile and its (mt, nt), without
-// divisions after init.
+// Walks a CTA's local units: stage kb, tile and its (mt, nt); divisions only
+// at tile boundaries.
 struct WorkPos {
   int j, kb, tile, nt, mt;
   __device__ __forceinline__ void set_tile(int t, const Sched& s) {
     tile = t;
-    mt = t / s.NT;
-    nt = t - mt * s.NT;
+    s.tile_mn(t, mt, nt);
   }
   __device__ __forceinline__ void init(int j0, const Sched& s) {
     j = j0;
@@ -228,18 +242,7 @@ struct WorkPos {
     }
     if (++kb == s.KBS) {
       kb = 0;
-      if (j < s.dp_units) {  // next data-parallel tile: tile + C
-        tile += s.C;
-        nt += s.C_nt;
-        mt += s.C_mt;
-      } else {
-        ++tile;
-        ++nt;
-      }
-      if (nt >= s.NT) {
-        nt -= s.NT;
-        ++mt;
-      }
+      set_tile(j < s.dp_units ? tile + s.C : tile + 1, s);
     }
   }
 };
@@ -284,7 +287,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   const int KB = p.KB, NT = p.NT;
   const int KBS = KB / SB;  // stages per tile (KB is even)
   Sched sch;
-  sch.init(MT * NT, KBS, NT, (int)gridDim.x, (int)blockIdx.x);
+  sch.init(MT, KBS, NT, p.group_m, (int)gridDim.x, (int)blockIdx.x);
   const int n_local = sch.n_local;
 
   if (threadIdx.x == 0) {
@@ -495,8 +498,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     for (int u = 0; u < n_local; acc.next<2>()) {
       const int tile = sch.tile_of(u);
       const int seg_end = sch.seg_end(u);
-      const int mt = tile / NT;
-      const int nt = tile - mt * NT;
+      int mt, nt;
+      sch.tile_mn(tile, mt, nt);
       const int n = nt * kBlockN + f;
       int rows_here = p.M - mt * NTOK;
       if (p.rows_valid != nullptr) rows_here = cmin(rows_here, *p.rows_valid - mt * NTOK);
