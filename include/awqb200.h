@@ -80,6 +80,13 @@ int awqb_gemm_workspace_bytes_ex(int64_t M, int64_t K, int64_t N, int64_t G, int
 int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
                  const void* blob, const void* bias, void* y, void* workspace,
                  int64_t workspace_bytes, int ntok, int64_t ctas, void* stream);
+/* The launch awqb_gemm / awqb_gemm_ex would make for these arguments: token
+ * tile, CTA count, and cluster size (1 = stream-K with the reduction through
+ * the workspace; >= 2 = one tile per cluster of that many CTAs, reduced
+ * through distributed shared memory). Diagnostics; no counterpart in the
+ * reference. */
+int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, int* ntok_out,
+                   int64_t* ctas_out, int* cluster_out);
 
 /* GEMM for callers that cannot provide or allocate device memory: a host that
  * owns every device byte through its own arena, or code that must never call

@@ -31,6 +31,8 @@ _SIGNATURES = {
     "awqb_dequant": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp]),
     "awqb_gemm_workspace_bytes": (c_int, [c_i64, c_i64, c_i64, c_i64, c_i64p]),
     "awqb_gemm_workspace_bytes_ex": (c_int, [c_i64, c_i64, c_i64, c_i64, c_int, c_i64, c_i64p]),
+    "awqb_gemm_plan": (c_int, [c_i64, c_i64, c_i64, c_i64, c_int, c_i64, ctypes.POINTER(c_int), c_i64p,
+                               ctypes.POINTER(c_int)]),
     "awqb_gemm": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "awqb_gemm_ex": (
         c_int,

@@ -5,6 +5,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "awqb200.h"
@@ -111,6 +113,7 @@ struct Plan {
   int NT, KB, MT;
   int64_t ctas;
   int64_t cnt_bytes, part_bytes;
+  int cluster_s;  // >= 2: cluster split-K launch (one tile per cluster of cluster_s CTAs)
 };
 
 int64_t round_up(int64_t a, int64_t b) { return (a + b - 1) / b * b; }
@@ -121,7 +124,52 @@ constexpr int64_t kCounterBytes = 2 * 4 * kMaxCtas;
 
 bool valid_group(int64_t G) { return G == 32 || G == 64 || (G >= 128 && G % 128 == 0); }
 
-int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, Plan* pl) {
+// How many clusters of S GEMM CTAs (one CTA per SM) the device runs at once;
+// cached per device. Every instantiation of the kernel needs nearly all of an
+// SM's shared memory, so one representative answers for all of them.
+int max_active_clusters(int S) {
+  static std::atomic<int> cache[kMaxDevices][9];
+  static std::once_flag init_flag;
+  std::call_once(init_flag, [] {
+    for (auto& row : cache)
+      for (auto& v : row) v.store(-1);
+  });
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices || S < 1 || S > 8) return 0;
+  int v = cache[dev][S].load();
+  if (v >= 0) return v;
+  using Cfg = GemmCfg<16, 1>;
+  auto kern = awq_gemm_kernel<__nv_bfloat16, 16, 1>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(S * 64));
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[dev][S].store(n);
+  return n;
+}
+
+// allow_cluster: a dense GEMM whose tiles fill at most half the SMs runs as
+// cluster split-K (each tile's stages split over a cluster of S CTAs whose
+// partials are reduced through distributed shared memory) when all T clusters
+// fit on the device at once.
+int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, Plan* pl,
+              bool allow_cluster = false) {
   AWQB_REQUIRE(M >= 0 && K > 0 && N > 0, kInvalidArgument, "bad GEMM sizes M=%lld K=%lld N=%lld",
                (long long)M, (long long)K, (long long)N);
   AWQB_REQUIRE(valid_group(G), kUnsupported, "group size %lld not supported (32, 64 or a multiple of 128)",
@@ -142,7 +190,28 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   pl->MT = (int)((M + pl->ntok - 1) / pl->ntok);
   const int64_t U = (int64_t)pl->MT * pl->NT * (pl->KB / stage_blocks(pl->ntok));
   int64_t c = ctas > 0 ? ctas : device_sm_count();
-  if (ctas <= 0) {
+  pl->cluster_s = 1;
+  if (ctas <= 0 && allow_cluster) {
+    const int64_t tiles = (int64_t)pl->MT * pl->NT;
+    const int64_t kbs = pl->KB / stage_blocks(pl->ntok);
+    if (tiles >= 1 && 2 * tiles <= c) {
+      int64_t S = std::min<int64_t>(std::min<int64_t>(8, c / tiles), kbs);
+      while (S >= 2 && max_active_clusters((int)S) < tiles) --S;
+      if (S >= 2) {
+        // Cluster split-K saves the global reduction (more the more rows it
+        // reduces and the more contributors stream-K would give each tile) but
+        // streams on tiles * S CTAs instead of all of them. Extra stages a CTA
+        // streams, in hundredths, against a threshold measured on B200 over the
+        // Llama-3 8B / 70B (TP 1..8) decode shapes (one stage ~0.48 us).
+        const int64_t extra = ((kbs + S - 1) / S) * 100 - tiles * kbs * 100 / c;
+        const int64_t rows = std::min<int64_t>(M, pl->ntok);
+        const int64_t limit = rows <= 8 ? 115 : rows <= 16 ? 210 : rows <= 32 ? 310 : 420;
+        if (extra <= limit || tiles <= 20) pl->cluster_s = (int)S;
+      }
+    }
+    if (pl->cluster_s > 1) c = tiles * pl->cluster_s;
+  }
+  if (ctas <= 0 && pl->cluster_s == 1) {
     // Larger token tiles make each split tile's partials bigger to reduce:
     // cap the contributors per tile.
     const int64_t tiles = (int64_t)pl->MT * pl->NT;
@@ -170,6 +239,7 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
 // and is read at kernel start.
 template <typename T, int NTOK, int GPB>
 int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, bool pdl, cudaStream_t stream) {
+  AWQB_REQUIRE(p.cluster_s <= 1 || ctas % p.cluster_s == 0, kInvalidArgument, "grid not a multiple of the cluster");
   using Cfg = GemmCfg<NTOK, GPB>;
   auto kern = awq_gemm_kernel<T, NTOK, GPB>;
   static bool attr_set[kMaxDevices] = {};
@@ -184,11 +254,22 @@ int launch_t(const CUtensorMap& tm, const GemmParams& p, int64_t ctas, bool pdl,
   cfg.blockDim = dim3(Cfg::kThreads);
   cfg.dynamicSmemBytes = Cfg::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.cluster_s > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = (unsigned)p.cluster_s;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = na;
   AWQB_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, p));
   return kOk;
 }
@@ -223,7 +304,7 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
                "dtype %d is not fp16 (0) or bf16 (1)", dtype);
   Plan pl;
-  int st = make_plan(M, K, N, G, ntok, ctas, &pl);
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true);
   if (st != kOk) return st;
   if (M == 0) return kOk;
   AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
@@ -259,6 +340,7 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.err = err;
   p.x3d = is3d;
   p.group_m = raster_group_m(K, N, p.tile_expert != nullptr);
+  p.cluster_s = pl.cluster_s;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, true, s);
@@ -272,7 +354,7 @@ using namespace awqb;
 extern "C" int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t G,
                                          int64_t* bytes) {
   Plan pl;
-  int st = make_plan(M, K, N, G, 0, 0, &pl);
+  int st = make_plan(M, K, N, G, 0, 0, &pl, true);
   if (st != kOk) return st;
   AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
   *bytes = pl.cnt_bytes + pl.part_bytes;
@@ -282,10 +364,23 @@ extern "C" int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_
 extern "C" int awqb_gemm_workspace_bytes_ex(int64_t M, int64_t K, int64_t N, int64_t G, int ntok,
                                             int64_t ctas, int64_t* bytes) {
   Plan pl;
-  int st = make_plan(M, K, N, G, ntok, ctas, &pl);
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true);
   if (st != kOk) return st;
   AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
   *bytes = pl.cnt_bytes + pl.part_bytes;
+  return kOk;
+}
+
+extern "C" int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas,
+                              int* ntok_out, int64_t* ctas_out, int* cluster_out) {
+  Plan pl;
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(ntok_out != nullptr && ctas_out != nullptr && cluster_out != nullptr, kInvalidArgument,
+               "null output pointer");
+  *ntok_out = pl.ntok;
+  *ctas_out = pl.ctas;
+  *cluster_out = pl.cluster_s;
   return kOk;
 }
 
@@ -346,7 +441,7 @@ extern "C" int64_t awqb_gemm_noalloc_scratch_bytes(void) { return kNoAllocScratc
 extern "C" int awqb_gemm_noalloc(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
                                  const void* blob, const void* bias, void* y, void* stream) {
   Plan pl;
-  int st = make_plan(M, K, N, G, 0, 0, &pl);
+  int st = make_plan(M, K, N, G, 0, 0, &pl, true);
   if (st != kOk) return st;
   if (M == 0) return kOk;
   const int64_t need = pl.cnt_bytes + pl.part_bytes;

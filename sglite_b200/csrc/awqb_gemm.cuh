@@ -86,6 +86,8 @@ struct GemmParams {
   uint32_t* err;                // device error word
   int32_t x3d;                  // X tensor map is 3-D {64, rows, K/64}: one load per stage
   int32_t group_m;              // token tiles per raster group (>= 1)
+  int32_t cluster_s;            // >= 2: launched in clusters of cluster_s CTAs, one tile per
+                                //   cluster; its partials are reduced through DSMEM
 };
 
 template <int NTOK, int GPB>
@@ -516,7 +518,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       const bool split = ncontrib > 1;
       // The owner holds the tile's first unit. The tile runs past its range, so
       // this is its last segment and the other TMEM accumulator buffer is free.
-      const bool owner = split && c_first == (int)blockIdx.x;
+      const bool owner = split && c_first == (int)blockIdx.x && p.cluster_s <= 1;
       // A split tile is the last segment of its first contributor, so each CTA
       // owns at most one: the tile's counters are indexed by that contributor.
       int32_t* const cnt = p.ws_cnt + 2 * c_first;
@@ -625,6 +627,26 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
         }
       };
 
+      if (split && p.cluster_s > 1) {
+        // Cluster split-K: this tile is the CTA's only segment, so the load ring
+        // is idle. The partial goes to shared memory as [row][128 features]; the
+        // cluster reduces it after the final barrier (kernel end).
+        float* sp = reinterpret_cast<float*>(lring) + f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < ncols; c0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(t_addr + c0, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (c0 + c < rows_here) sp[(c0 + c) * 128] = __uint_as_float(v[c]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acc_empty[acc.idx]));
+        u = seg_end;
+        continue;
+      }
       const bool fast = split && named_bar_and(1, kEpiThreads, owner && pre);
       if (!split || fast) {
         // Whole tile, or an owner with its peers' sum ready: final values now.
@@ -864,6 +886,40 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   }
 
   __syncthreads();
+  if (p.cluster_s > 1) {
+    // Cluster split-K finale: every CTA of the cluster holds a partial of the
+    // same tile in shared memory ([row][128 features] fp32). Rank r sums the
+    // features [128 r / S, 128 (r+1) / S) over the S partials in rank order
+    // (deterministic), reading its peers' shared memory directly, and stores
+    // them; the second barrier keeps every CTA's shared memory alive until its
+    // peers have read it.
+    cluster_sync_all();
+    if (n_local > 0) {
+      const int S = p.cluster_s;
+      const int rank = (int)cluster_ctarank();
+      int mt, nt;
+      sch.tile_mn(sch.tile_of(0), mt, nt);
+      const int rows_here = cmax(0, cmin(NTOK, p.M - mt * NTOK));
+      const int f0 = rank * 128 / S;
+      const int nf = (rank + 1) * 128 / S - f0;
+      const uint32_t base_sm = smem_u32(lring);
+      for (int e = threadIdx.x; e < nf * rows_here; e += Cfg::kThreads) {
+        const int c = e / nf;
+        const int f = f0 + (e - c * nf);
+        const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < 8; ++r)
+          if (r < S) v += ld_dsmem_f32(mapa_shared(off, (uint32_t)r));
+        const int n = nt * kBlockN + f;
+        if (n < p.N) {
+          if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
+          reinterpret_cast<T*>(p.y)[(int64_t)(mt * NTOK + c) * p.ldy + n] = (T)v;
+        }
+      }
+    }
+    cluster_sync_all();
+  }
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);

@@ -166,6 +166,13 @@ def gemm_workspace_bytes(M: int, K: int, N: int, G: int, ntok: int = 0, ctas: in
     return out.value
 
 
+def gemm_plan(M: int, K: int, N: int, G: int, ntok: int = 0, ctas: int = 0) -> Dict[str, int]:
+    """The launch the GEMM makes for these sizes: token tile, CTAs, cluster size."""
+    t, c, s = ctypes.c_int(0), c_i64(0), ctypes.c_int(0)
+    call("awqb_gemm_plan", M, K, N, G, ntok, ctas, ctypes.byref(t), ctypes.byref(c), ctypes.byref(s))
+    return {"ntok": t.value, "ctas": c.value, "cluster": s.value}
+
+
 # ---------------------------------------------------------------- GEMM
 def gemm(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
          bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,

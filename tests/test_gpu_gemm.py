@@ -148,3 +148,22 @@ def test_gemm_data_parallel_waves(cuda, ntok):
     ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
     assert rel_err(y, ref) <= TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("K,N,M", [(4096, 4096, 1), (4096, 4096, 33), (4096, 4096, 64), (8192, 1280, 5), (1024, 8192, 16)])
+def test_gemm_cluster_split_k(cuda, K, N, M):
+    """Few feature tiles: each tile's stages are split over a thread-block
+    cluster and reduced through distributed shared memory. Checked against the
+    oracle and against the stream-K launch (reduction through the workspace)."""
+    G = 128
+    plan = ops.gemm_plan(M, K, N, G)
+    assert plan["cluster"] >= 2, plan
+    w, x, blob = _setup(cuda, M, K, N, G, torch.bfloat16, seed=K + N + M)
+    y = ops.gemm(x.to(cuda), blob, K, N, G)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y, ref) <= TOL
+    y_sk = ops.gemm(x.to(cuda), blob, K, N, G, ctas=torch.cuda.get_device_properties(cuda).multi_processor_count)
+    assert ops.gemm_plan(M, K, N, G, ctas=1)["cluster"] == 1
+    assert rel_err(y, y_sk.float()) <= TOL
+    assert torch.equal(y, ops.gemm(x.to(cuda), blob, K, N, G))  # deterministic
+    assert ops.device_error() == 0
