@@ -222,16 +222,19 @@ def run_ours(args):
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    comm = None
+    comm = ex = None
     if world > 1:
         from datetime import timedelta
 
-        from sglite_b200.distributed import init_nccl
+        from sglite_b200.distributed import init_nccl, init_peer_exchange
 
         dist.init_process_group("gloo", timeout=timedelta(seconds=120))
         max_bytes = max(MS) * 4096 * 2
         comm = init_nccl(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
                          max_size_bytes=max_bytes)
+        if args.allreduce == "fused":
+            ex = init_peer_exchange(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
+                                    max_rows=max(MS), max_n=4096)
 
     cfg = AWQB200Config(4, G, True)
     method = cfg.get_linear_method()
@@ -253,6 +256,10 @@ def run_ours(args):
     def step():
         for (n, M) in order:
             w = layers[n]
+            if ex is not None and n in ROW_PARALLEL:  # GEMM + all-reduce in one kernel over peer memory
+                ex.gemm_allreduce(xs[(n, M)], w["qweight"], w["_input_size"], w["_output_size"], G,
+                                  out=ys[(n, M)])
+                continue
             ops.gemm(xs[(n, M)], w["qweight"], w["_input_size"], w["_output_size"], G, out=ys[(n, M)])
             if comm is not None and n in ROW_PARALLEL:
                 comm.all_reduce(ys[(n, M)])
@@ -317,9 +324,13 @@ def run_ours(args):
     def e2e_step():
         for (n, M) in order:
             xd = hx[(n, M)].to(dev, non_blocking=True)
-            y = method.apply_weights(layers[n], xd)
-            if comm is not None and n in ROW_PARALLEL:
-                comm.all_reduce(y)
+            if ex is not None and n in ROW_PARALLEL:
+                w = layers[n]
+                y = ex.gemm_allreduce(xd, w["qweight"], w["_input_size"], w["_output_size"], G)
+            else:
+                y = method.apply_weights(layers[n], xd)
+                if comm is not None and n in ROW_PARALLEL:
+                    comm.all_reduce(y)
             hy[(n, M)].copy_(y, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -363,6 +374,8 @@ def run_ours(args):
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": len(order) * args.steps,
         "graph": "one CUDA-graph replay per step (16 GEMM launches)",
+        "allreduce": ("none" if world == 1 else
+                      "fused into the row-parallel GEMM over peer memory" if ex is not None else "NCCL"),
         "clocks": clk.summary(),
         "device_error": err,
     }
@@ -372,6 +385,8 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
     del graph, graph_g
     torch.cuda.synchronize()
+    if ex is not None:
+        ex.destroy()
     if comm is not None:
         comm.destroy()
     if world > 1:
@@ -493,15 +508,18 @@ def run_tp70b(args):
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    comm = None
+    comm = ex = None
     if world > 1:
         from datetime import timedelta
 
-        from sglite_b200.distributed import init_nccl
+        from sglite_b200.distributed import init_nccl, init_peer_exchange
 
         dist.init_process_group("gloo", timeout=timedelta(seconds=120))
         comm = init_nccl(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
                          max_size_bytes=256 * 8192 * 2)
+        if args.allreduce == "fused":
+            ex = init_peer_exchange(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
+                                    max_rows=64, max_n=8192)
     full = {"qkv": (8192, 10240), "o": (8192, 8192), "gate_up": (8192, 57344), "down": (28672, 8192)}
     loc = {n: ((K // world, N) if n in ROW_PARALLEL else (K, N // world)) for n, (K, N) in full.items()}
     ws = {}
@@ -515,6 +533,9 @@ def run_tp70b(args):
 
         def layer():
             for n, (K, N) in loc.items():
+                if ex is not None and n in ROW_PARALLEL and M <= ex.max_rows:
+                    ex.gemm_allreduce(xs[n], ws[n]["qweight"], K, N, G, out=ys[n])
+                    continue
                 ops.gemm(xs[n], ws[n]["qweight"], K, N, G, out=ys[n])
                 if comm is not None and n in ROW_PARALLEL:
                     comm.all_reduce(ys[n])
@@ -535,7 +556,11 @@ def run_tp70b(args):
         print(json.dumps({"workload": f"llama3.1_70b_awq_layer_tp{world} (config 3)", "metric": "TP-layer us",
                           "unit": "us", "n_gpus": world, "per_m": out,
                           "roofline": "max(weight bytes / measured HBM, flops / measured bf16 peak) + 2 ring all-reduces at 770 GB/s",
+                          "allreduce": ("fused GEMM + all-reduce over peer memory for M <= 64, NCCL above"
+                                        if ex is not None else "NCCL"),
                           "peak_kind": kind}), flush=True)
+    if ex is not None:
+        ex.destroy()
     if comm is not None:
         comm.destroy()
     if world > 1:
@@ -584,6 +609,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe", "gemm"],
                     help="decode (default, the contract line) or another BASELINE config")
+    ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
+                    help="row-parallel all-reduce at N > 1: fused into the GEMM over peer memory, or NCCL")
     ap.add_argument("--shape", default="4096x28672x1", help="KxNxM for --workload gemm")
     ap.add_argument("--fp16", action="store_true", help="fp16 activations for --workload gemm")
     args = ap.parse_args()

@@ -169,6 +169,37 @@ int awqb_nccl_symmetric_buffer(void* comm, void** ptr, int64_t* bytes);
 int awqb_nccl_all_reduce(void* comm, void* buf, int64_t count, int dtype, void* stream);
 int awqb_nccl_destroy(void* comm);
 
+/* ------------------------------------------------------------------------
+ * Row-parallel GEMM fused with its all-reduce over peer memory (NVLink).
+ * Replaces, for small M, the pair RowParallelLinear.forward
+ * (layers/linear.py:189-194) = quantised GEMM + PyNCCLCommunicator.all_reduce
+ * (kernels/csrc/src/pynccl.cu:96-138): every rank computes its K-slice
+ * product and writes each finished value, as one 8-byte {fp32, call tag} word,
+ * into every rank's landing buffer; each rank waits for the world words of its
+ * values (no fences or flags: the tag travels with the value), sums them in
+ * rank order (identical bits on all ranks), adds the bias once and stores
+ * y [M][N] in the activation dtype. One kernel, no NCCL call.
+ *
+ * Set-up, once per rank of the group (collective in spirit: every rank must do
+ * it): awqb_tp_exchange_create allocates this rank's exchange buffer
+ * (cudaMalloc, 16 * world * max_rows * max_n bytes + 256) on the current
+ * device; exchange the awqb_tp_exchange_handle bytes of all ranks (any host
+ * channel), then awqb_tp_exchange_open(ctx, handles of ranks 0..world-1 back to
+ * back). Every rank must then issue the same sequence of awqb_gemm_allreduce
+ * calls with the same M, K, N, G (a collective); M <= max_rows, N <= max_n.
+ * The kernel waits (bounded, 2 s) for its peers' tiles: a rank that does not
+ * take part turns into a device error (awqb_device_error), not a hang. The
+ * context may be used inside CUDA graphs (no host state changes per call).
+ */
+int awqb_tp_exchange_handle_bytes(int64_t* bytes);
+int awqb_tp_exchange_create(int rank, int world, int64_t max_rows, int64_t max_n, void** ctx);
+int awqb_tp_exchange_handle(void* ctx, void* handle_out);
+int awqb_tp_exchange_open(void* ctx, const void* handles);
+int awqb_tp_exchange_destroy(void* ctx);
+int awqb_gemm_allreduce(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                        const void* blob, const void* bias, void* y, void* workspace,
+                        int64_t workspace_bytes, void* ctx, void* stream);
+
 /* Device-side error word (bits set when a bounded wait inside a kernel gave
  * up). Both calls synchronise the current device. */
 int awqb_device_error(uint32_t* out);

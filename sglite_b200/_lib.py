@@ -58,6 +58,13 @@ _SIGNATURES = {
     "awqb_nccl_symmetric_buffer": (c_int, [c_vp, ctypes.POINTER(c_vp), c_i64p]),
     "awqb_nccl_all_reduce": (c_int, [c_vp, c_vp, c_i64, c_int, c_vp]),
     "awqb_nccl_destroy": (c_int, [c_vp]),
+    "awqb_tp_exchange_handle_bytes": (c_int, [c_i64p]),
+    "awqb_tp_exchange_create": (c_int, [c_int, c_int, c_i64, c_i64, ctypes.POINTER(c_vp)]),
+    "awqb_tp_exchange_handle": (c_int, [c_vp, c_vp]),
+    "awqb_tp_exchange_open": (c_int, [c_vp, c_vp]),
+    "awqb_tp_exchange_destroy": (c_int, [c_vp]),
+    "awqb_gemm_allreduce": (
+        c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp]),
     "awqb_device_error": (c_int, [c_u32p]),
     "awqb_clear_device_error": (c_int, []),
 }

@@ -6,6 +6,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <mutex>
 
@@ -168,8 +169,10 @@ int max_active_clusters(int S) {
 // cluster split-K (each tile's stages split over a cluster of S CTAs whose
 // partials are reduced through distributed shared memory) when all T clusters
 // fit on the device at once.
+// prefer_cluster: take cluster split-K whenever it fits (the fused all-reduce,
+// whose per-value exchange is cheapest with the cluster's all-thread finale).
 int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, Plan* pl,
-              bool allow_cluster = false) {
+              bool allow_cluster = false, bool prefer_cluster = false) {
   AWQB_REQUIRE(M >= 0 && K > 0 && N > 0, kInvalidArgument, "bad GEMM sizes M=%lld K=%lld N=%lld",
                (long long)M, (long long)K, (long long)N);
   AWQB_REQUIRE(valid_group(G), kUnsupported, "group size %lld not supported (32, 64 or a multiple of 128)",
@@ -206,7 +209,7 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
         const int64_t extra = ((kbs + S - 1) / S) * 100 - tiles * kbs * 100 / c;
         const int64_t rows = std::min<int64_t>(M, pl->ntok);
         const int64_t limit = rows <= 8 ? 115 : rows <= 16 ? 210 : rows <= 32 ? 310 : 420;
-        if (extra <= limit || tiles <= 20) pl->cluster_s = (int)S;
+        if (extra <= limit || tiles <= 20 || prefer_cluster) pl->cluster_s = (int)S;
       }
     }
     if (pl->cluster_s > 1) c = tiles * pl->cluster_s;
@@ -229,7 +232,8 @@ int make_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas
   // Counters live in a fixed region at the start of every workspace, so calls
   // with different plans sharing one workspace never write partials over them.
   pl->cnt_bytes = kCounterBytes;
-  pl->part_bytes = c * 2 * 128 * (int64_t)pl->ntok * 4;
+  // Cluster split-K reduces through shared memory: no partials in the workspace.
+  pl->part_bytes = pl->cluster_s > 1 ? 0 : c * 2 * 128 * (int64_t)pl->ntok * 4;
   return kOk;
 }
 
@@ -298,13 +302,31 @@ int launch_n(const CUtensorMap& tm, const GemmParams& p, const Plan& pl, bool pd
   return kUnsupported;
 }
 
+// Peer-memory exchange of one tensor-parallel group, as seen by one rank: one
+// device allocation per rank holds [2 parities][world][rows][max_n] landing
+// words (8 bytes: fp32 value + call tag) and a call counter pair; every rank
+// maps every peer's allocation (CUDA IPC).
+struct TpExchange {
+  int rank = 0, world = 1, device = 0;
+  int64_t rows = 0, max_n = 0;
+  int64_t half_words = 0;    // landing words per parity
+  void* local = nullptr;     // this rank's allocation
+  void* base[8] = {};        // every rank's allocation as mapped here
+  bool opened = false;
+  int64_t land_bytes() const { return 2 * half_words * 8; }
+  int64_t total_bytes() const { return land_bytes() + 256; }
+  uint2* land(int r) const { return static_cast<uint2*>(base[r]); }
+  int32_t* epoch() const { return reinterpret_cast<int32_t*>(static_cast<uint8_t*>(local) + land_bytes()); }
+};
+
 int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
               const void* blob, const void* bias, void* y, void* workspace,
-              int64_t workspace_bytes, int ntok, int64_t ctas, void* stream) {
+              int64_t workspace_bytes, int ntok, int64_t ctas, void* stream,
+              const TpExchange* tp = nullptr) {
   AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
                "dtype %d is not fp16 (0) or bf16 (1)", dtype);
   Plan pl;
-  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true);
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true, tp != nullptr);
   if (st != kOk) return st;
   if (M == 0) return kOk;
   AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
@@ -341,6 +363,18 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.x3d = is3d;
   p.group_m = raster_group_m(K, N, p.tile_expert != nullptr);
   p.cluster_s = pl.cluster_s;
+  if (tp != nullptr) {
+    AWQB_REQUIRE(tp->opened, kInvalidArgument, "exchange not opened (awqb_tp_exchange_open)");
+    AWQB_REQUIRE(M <= tp->rows && N <= tp->max_n, kInvalidArgument,
+                 "fused all-reduce sized for M <= %lld, N <= %lld (got M=%lld, N=%lld)", (long long)tp->rows,
+                 (long long)tp->max_n, (long long)M, (long long)N);
+    p.tp_world = tp->world;
+    p.tp_rank = tp->rank;
+    p.tp_rows = (int32_t)tp->rows;
+    p.tp_half = tp->half_words;
+    for (int r = 0; r < tp->world; ++r) p.tp_land[r] = tp->land(r);
+    p.tp_epoch = tp->epoch();
+  }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, true, s);
@@ -554,4 +588,92 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, false, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, false, s);
+}
+
+// ---------------------------------------------------------------------------
+// Fused row-parallel GEMM + all-reduce over peer memory.
+extern "C" int awqb_tp_exchange_create(int rank, int world, int64_t max_rows, int64_t max_n, void** ctx) {
+  using namespace awqb;
+  AWQB_REQUIRE(ctx != nullptr, kInvalidArgument, "ctx is null");
+  AWQB_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, kInvalidArgument,
+               "rank %d / world %d (1..8 ranks)", rank, world);
+  AWQB_REQUIRE(max_rows >= 1 && max_rows <= 256 && max_n >= 8 && max_n % 8 == 0, kInvalidArgument,
+               "max_rows must be 1..256 and max_n a positive multiple of 8");
+  auto* t = new TpExchange();
+  t->rank = rank;
+  t->world = world;
+  t->rows = max_rows;
+  t->max_n = max_n;
+  t->half_words = (int64_t)world * max_rows * max_n;
+  cudaError_t e = cudaGetDevice(&t->device);
+  if (e == cudaSuccess) e = cudaMalloc(&t->local, (size_t)t->total_bytes());
+  if (e == cudaSuccess) e = cudaMemset(t->local, 0, (size_t)t->total_bytes());
+  if (e != cudaSuccess) {
+    if (t->local) cudaFree(t->local);
+    delete t;
+    AWQB_CUDA(e);
+  }
+  t->base[rank] = t->local;
+  *ctx = t;
+  return kOk;
+}
+
+extern "C" int awqb_tp_exchange_handle(void* ctx, void* handle_out) {
+  using namespace awqb;
+  AWQB_REQUIRE(ctx != nullptr && handle_out != nullptr, kInvalidArgument, "null pointer");
+  auto* t = static_cast<TpExchange*>(ctx);
+  cudaIpcMemHandle_t h;
+  AWQB_CUDA(cudaIpcGetMemHandle(&h, t->local));
+  memcpy(handle_out, &h, sizeof(h));
+  return kOk;
+}
+
+extern "C" int awqb_tp_exchange_open(void* ctx, const void* handles) {
+  using namespace awqb;
+  AWQB_REQUIRE(ctx != nullptr && handles != nullptr, kInvalidArgument, "null pointer");
+  auto* t = static_cast<TpExchange*>(ctx);
+  AWQB_REQUIRE(!t->opened, kInvalidArgument, "exchange already opened");
+  for (int r = 0; r < t->world; ++r) {
+    if (r == t->rank) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof(h), sizeof(h));
+    void* ptr = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int q = 0; q < r; ++q)
+        if (q != t->rank && t->base[q]) cudaIpcCloseMemHandle(t->base[q]);
+      AWQB_CUDA(e);
+    }
+    t->base[r] = ptr;
+  }
+  t->opened = true;
+  return kOk;
+}
+
+extern "C" int awqb_tp_exchange_handle_bytes(int64_t* bytes) {
+  using namespace awqb;
+  AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
+  *bytes = (int64_t)sizeof(cudaIpcMemHandle_t);
+  return kOk;
+}
+
+extern "C" int awqb_tp_exchange_destroy(void* ctx) {
+  using namespace awqb;
+  if (ctx == nullptr) return kOk;
+  auto* t = static_cast<TpExchange*>(ctx);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < t->world; ++r)
+    if (r != t->rank && t->base[r]) cudaIpcCloseMemHandle(t->base[r]);
+  if (t->local) cudaFree(t->local);
+  delete t;
+  return kOk;
+}
+
+extern "C" int awqb_gemm_allreduce(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                                   const void* blob, const void* bias, void* y, void* workspace,
+                                   int64_t workspace_bytes, void* ctx, void* stream) {
+  using namespace awqb;
+  AWQB_REQUIRE(ctx != nullptr, kInvalidArgument, "ctx is null");
+  return gemm_impl(x, M, K, N, G, dtype, blob, bias, y, workspace, workspace_bytes, 0, 0, stream,
+                   static_cast<const TpExchange*>(ctx));
 }

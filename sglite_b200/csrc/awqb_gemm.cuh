@@ -88,6 +88,16 @@ struct GemmParams {
   int32_t group_m;              // token tiles per raster group (>= 1)
   int32_t cluster_s;            // >= 2: launched in clusters of cluster_s CTAs, one tile per
                                 //   cluster; its partials are reduced through DSMEM
+  // Fused all-reduce across tensor-parallel ranks (tp_world >= 2, or 1 to run
+  // the exchange against itself): every final value goes as an 8-byte {fp32,
+  // call tag} word into every rank's landing buffer; each rank waits for the
+  // tp_world words of each of its values and sums them in rank order.
+  int32_t tp_world, tp_rank;
+  int32_t tp_rows;              // landing rows per slot (>= M)
+  int64_t tp_half;              // words per parity half of a landing buffer
+  uint2* tp_land[8];            // per rank (peer-mapped): landing words, [2][world][rows][N]
+  int32_t* tp_epoch;            // this rank's call counter (tag = epoch + 1, buffer = epoch & 1)
+                                //   and the count of CTAs done with the call
 };
 
 template <int NTOK, int GPB>
@@ -121,7 +131,7 @@ struct GemmCfg {
   static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK + (kATmem ? kSD * kAStageCols : 0)));
   static_assert(kSD >= 2, "need two A stages");
   static_assert(kTmemCols <= 512, "TMEM over capacity");
-  static_assert((2 * kSL + 2 * kSD + 6) * 8 + 16 <= 512, "barrier area overflow");
+  static_assert((2 * kSL + 2 * kSD + 6) * 8 + 32 <= 512, "barrier area overflow");
   static_assert(kSL >= 2, "not enough shared memory for two load stages");
   static_assert(kSmemBytes <= 232448, "shared memory over the sm_100 per-CTA limit");
   static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "MMA N must be 16..256 step 16");
@@ -249,9 +259,66 @@ struct WorkPos {
   }
 };
 
+// Fused all-reduce: one final value, as a tagged word, to every rank's landing
+// buffer (out of line: keeps the epilogue's registers free).
+__device__ __noinline__ void tp_put(uint2* const* lands, int world, int64_t off, float v, uint32_t tag) {
+  for (int d = 0; d < world; ++d) st_tagged_sys(lands[d] + off, v, tag);
+}
+
+// Fused all-reduce, final step for one feature column of a tile: wait until
+// each of the world ranks' words for rows 0..rows-1 carries this call's tag,
+// sum them in rank order, add the bias and store. land points at rank 0's word
+// of row 0 (slots are rows_cap * ld words apart); bounded wait.
+template <typename T>
+__device__ __forceinline__ void tp_finalize_column(const uint2* land, T* y, int64_t ldy, int ld, int rows_cap,
+                                                int world, int rows, float bias, uint32_t tag, uint32_t* err) {
+  // 8 words in flight: rows_per = 8 / world rows per batch, each with all
+  // world ranks' words, summed in rank order.
+  const int rows_per = world >= 8 ? 1 : 8 / world;
+  uint64_t t0 = 0;
+  for (int c0 = 0; c0 < rows; c0 += rows_per) {
+    uint2 w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int cr = i / world;
+      const int r = i - cr * world;
+      const bool live = cr < rows_per && c0 + cr < rows;
+      w[i] = live ? ld_tagged_sys(land + ((int64_t)r * rows_cap + c0 + cr) * ld) : make_uint2(0u, tag);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (w[i].y == tag) continue;
+      const int cr = i / world;
+      const int r = i - cr * world;
+      const uint2* wp = land + ((int64_t)r * rows_cap + c0 + cr) * ld;
+      do {
+        if (t0 == 0) {
+          t0 = globaltimer_ns();
+        } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+          atomicOr(err, 8u);  // kErrWaitEpilogue
+          return;
+        }
+        w[i] = ld_tagged_sys(wp);
+      } while (w[i].y != tag);
+    }
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int cr = i / world;
+      const int r = i - cr * world;
+      if (cr >= rows_per || c0 + cr >= rows) break;
+      v += __uint_as_float(w[i].x);
+      if (r == world - 1) {
+        y[(int64_t)(c0 + cr) * ldy] = (T)(v + bias);
+        v = 0.f;
+      }
+    }
+  }
+}
+
 template <typename T, int NTOK, int GPB>
 __global__ void __maxnreg__(80)
-awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) {
+awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ GemmParams p) {
   using Cfg = GemmCfg<NTOK, GPB>;
   using DQ = DqTraits<T>;
   constexpr int SL = Cfg::kSL;
@@ -276,6 +343,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(red_bar + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_flag = reinterpret_cast<volatile int*>(s_tmem + 2);  // [2]
+  volatile uint32_t* s_tpe = s_tmem + 4;  // fused all-reduce: this call's counter value
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -496,6 +564,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     const int etid = threadIdx.x - Cfg::kEpiWarp0 * 32;
     constexpr int kEpiThreads = Cfg::kNumEpiWarps * 32;
     grid_dep_wait();  // outputs, workspace counters and partials belong to the previous grid until then
+    if (etid == 0) *s_tpe = p.tp_world > 0 ? (uint32_t)*reinterpret_cast<volatile int*>(p.tp_epoch) : 0u;
+    named_bar_sync(1, kEpiThreads);
     RingPos acc;
     for (int u = 0; u < n_local; acc.next<2>()) {
       const int tile = sch.tile_of(u);
@@ -595,6 +665,17 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
       // each (row_map) and its scale (row_scale) are read once per chunk by
       // lanes 0..15 and broadcast with shuffles (warp-uniform loop).
       auto store_row_vals = [&](int c0, const float* vals, int cnt) {
+        if (p.tp_world > 0) {  // fused all-reduce: tagged words to every rank's landing slot (no bias yet)
+          if (n >= p.N) return;
+          const uint32_t e = *s_tpe;
+          const int64_t base = (int64_t)(e & 1u) * p.tp_half +
+                               ((int64_t)p.tp_rank * p.tp_rows + mt * NTOK + c0) * p.N + n;
+          const int lim = cmin(cnt, rows_here - c0);
+#pragma unroll
+          for (int c = 0; c < 16; ++c)
+            if (c < lim) tp_put(p.tp_land, p.tp_world, base + (int64_t)c * p.N, vals[c], e + 1u);
+          return;
+        }
         if (p.row_map == nullptr && p.row_scale == nullptr) {  // dense GEMM: rows in order
           if (n >= p.N) return;
 #pragma unroll
@@ -625,6 +706,17 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
             reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
           }
         }
+      };
+      // Fused all-reduce, after this thread has written its final values of the
+      // tile to every rank: wait for each rank's word of each of its values
+      // (tag of this call), sum them in rank order, add the bias, store.
+      auto tp_finish = [&]() {
+        if (n >= p.N) return;
+        const uint32_t e = *s_tpe;
+        const float bv = p.bias != nullptr ? (float)reinterpret_cast<const T*>(p.bias)[n] : 0.f;
+        tp_finalize_column<T>(p.tp_land[p.tp_rank] + (int64_t)(e & 1u) * p.tp_half + (int64_t)mt * NTOK * p.N + n,
+                              reinterpret_cast<T*>(p.y) + (int64_t)mt * NTOK * p.ldy + n, p.ldy, p.N, p.tp_rows,
+                              p.tp_world, rows_here, bv, e + 1u, p.err);
       };
 
       if (split && p.cluster_s > 1) {
@@ -675,6 +767,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
           cnt[0] = 0;
           cnt[1] = 0;
         }
+        if (p.tp_world > 0) tp_finish();
       } else {
         // Take an arrival ticket. The last contributor to arrive reduces the
         // tile: it keeps its own partial in TMEM and waits for the others to
@@ -784,6 +877,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
               }
               store_row_vals(c0, sum, 8);
             }
+            if (p.tp_world > 0) tp_finish();
           }
           tc_fence_before();
           __syncwarp();
@@ -894,31 +988,81 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const GemmParams p) 
     // them; the second barrier keeps every CTA's shared memory alive until its
     // peers have read it.
     cluster_sync_all();
-    if (n_local > 0) {
-      const int S = p.cluster_s;
-      const int rank = (int)cluster_ctarank();
-      int mt, nt;
-      sch.tile_mn(sch.tile_of(0), mt, nt);
-      const int rows_here = cmax(0, cmin(NTOK, p.M - mt * NTOK));
-      const int f0 = rank * 128 / S;
-      const int nf = (rank + 1) * 128 / S - f0;
-      const uint32_t base_sm = smem_u32(lring);
-      for (int e = threadIdx.x; e < nf * rows_here; e += Cfg::kThreads) {
-        const int c = e / nf;
-        const int f = f0 + (e - c * nf);
-        const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
-        float v = 0.f;
+    const int S = p.cluster_s;
+    const int rank = (int)cluster_ctarank();
+    const int tile = sch.tile_of(0);
+    int mt, nt;
+    sch.tile_mn(tile, mt, nt);
+    const int rows_here = n_local > 0 ? cmax(0, cmin(NTOK, p.M - mt * NTOK)) : 0;
+    const int f0 = rank * 128 / S;
+    const int nf = (rank + 1) * 128 / S - f0;
+    const uint32_t tp_epoch = p.tp_world > 0 ? (uint32_t)*reinterpret_cast<volatile int*>(p.tp_epoch) : 0u;
+    const int tp_par = (int)(tp_epoch & 1u);
+    const uint32_t tp_tag = tp_epoch + 1u;
+    const uint32_t base_sm = smem_u32(lring);
+    for (int e = threadIdx.x; e < nf * rows_here; e += Cfg::kThreads) {
+      const int c = e / nf;
+      const int f = f0 + (e - c * nf);
+      const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
+      float v = 0.f;
 #pragma unroll
-        for (int r = 0; r < 8; ++r)
-          if (r < S) v += ld_dsmem_f32(mapa_shared(off, (uint32_t)r));
-        const int n = nt * kBlockN + f;
-        if (n < p.N) {
+      for (int r = 0; r < 8; ++r)
+        if (r < S) v += ld_dsmem_f32(mapa_shared(off, (uint32_t)r));
+      const int n = nt * kBlockN + f;
+      if (n < p.N) {
+        const int m = mt * NTOK + c;
+        if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's landing slot
+          const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
+          for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tp_tag);
+        } else {
           if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
-          reinterpret_cast<T*>(p.y)[(int64_t)(mt * NTOK + c) * p.ldy + n] = (T)v;
+          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)v;
+        }
+      }
+    }
+    if (p.tp_world > 0) {
+      // Each thread waits for every rank's word of the values it contributed,
+      // then sums them in rank order.
+      const uint2* land = p.tp_land[p.tp_rank] + (int64_t)tp_par * p.tp_half;
+      uint64_t t0 = 0;
+      bool ok = true;
+      for (int e = threadIdx.x; e < nf * rows_here && ok; e += Cfg::kThreads) {
+        const int c = e / nf;
+        const int n = nt * kBlockN + f0 + (e - c * nf);
+        if (n >= p.N) continue;
+        const int m = mt * NTOK + c;
+        float v = 0.f;
+        for (int r = 0; r < p.tp_world && ok; ++r) {
+          const uint2* wp = land + ((int64_t)r * p.tp_rows + m) * p.N + n;
+          uint2 w = ld_tagged_sys(wp);
+          while (w.y != tp_tag) {
+            if (t0 == 0) t0 = globaltimer_ns();
+            else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+              atomicOr(p.err, kErrWaitEpilogue);
+              ok = false;
+              break;
+            }
+            w = ld_tagged_sys(wp);
+          }
+          v += __uint_as_float(w.x);
+        }
+        if (ok) {
+          if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
+          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)v;
         }
       }
     }
     cluster_sync_all();
+  }
+  if (p.tp_world > 0 && threadIdx.x == 0) {
+    // The last CTA to finish advances this rank's call counter (the parity of
+    // the next fused call); the next kernel reads it after the grid boundary.
+    __threadfence();
+    if (atomicAdd(p.tp_epoch + 1, 1) == (int)gridDim.x - 1) {
+      p.tp_epoch[1] = 0;
+      __threadfence();
+      atomicAdd(p.tp_epoch, 1);
+    }
   }
   if (warp == 1) {
     tc_fence_after();

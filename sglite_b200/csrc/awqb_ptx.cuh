@@ -334,6 +334,30 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* addr) {
   asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
   return v;
 }
+// System scope (other GPUs over NVLink): release-add on a peer's flag, acquire
+// load of a local flag that peers add to, and a full fence.
+__device__ __forceinline__ void red_add_release_sys(int* addr, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// 8-byte {value, tag} words (single-copy atomic): a receiver that sees the tag
+// it expects also sees the value stored with it, with no fence on either side.
+__device__ __forceinline__ void st_tagged_sys(void* addr, float v, uint32_t tag) {
+  asm volatile("st.relaxed.sys.global.v2.b32 [%0], {%1, %2};" ::"l"(addr), "r"(__float_as_uint(v)), "r"(tag)
+               : "memory");
+}
+__device__ __forceinline__ uint2 ld_tagged_sys(const void* addr) {
+  uint2 r;
+  asm volatile("ld.relaxed.sys.global.v2.b32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(addr) : "memory");
+  return r;
+}
+
 // Acquire fence (gpu scope) for the thread that observed the final count.
 __device__ __forceinline__ void fence_acquire_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");

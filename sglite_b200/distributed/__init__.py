@@ -1,5 +1,8 @@
 """Tensor-parallel communication for the row-parallel projections.
 
+Two paths: NCCL (``init_nccl``, any size) and, for decode-sized M, the GEMM fused
+with its all-reduce over peer memory (``init_peer_exchange``).
+
 ``init_nccl`` follows the reference's ``init_pynccl`` (kernels/pynccl.py:50-83):
 rank 0 creates the NCCL unique id, the id travels over the CPU (gloo) process
 group with ``broadcast_object_list``, and every rank builds its communicator
@@ -89,4 +92,85 @@ def init_nccl(*, tp_rank: int, tp_size: int, tp_cpu_group, device: torch.device,
     return NcclCommunicator(tp_rank, tp_size, ids[0], device, max_size_bytes)
 
 
-__all__ = ["NcclCommunicator", "get_unique_id", "init_nccl"]
+class PeerExchange:
+    """Fused row-parallel GEMM + all-reduce over peer memory (one per TP rank).
+
+    Replaces, for M <= ``max_rows``, the reference's row-parallel pair: the
+    quantised GEMM followed by ``PyNCCLCommunicator.all_reduce``
+    (layers/linear.py:189-194, pynccl.cu:96-138). Every rank must call
+    ``gemm_allreduce`` in the same order with the same shapes.
+    """
+
+    def __init__(self, rank: int, world: int, device: torch.device, max_rows: int, max_n: int):
+        self.rank, self.world, self.device = rank, world, device
+        self.max_rows, self.max_n = max_rows, max_n
+        self._ctx = ctypes.c_void_p(0)
+        with _DeviceGuard(device):
+            call("awqb_tp_exchange_create", rank, world, max_rows, max_n, ctypes.byref(self._ctx))
+
+    def handle(self) -> bytes:
+        n = c_i64(0)
+        call("awqb_tp_exchange_handle_bytes", ctypes.byref(n))
+        buf = ctypes.create_string_buffer(n.value)
+        call("awqb_tp_exchange_handle", self._ctx, buf)
+        return buf.raw
+
+    def open(self, handles) -> None:
+        blob = b"".join(handles)
+        buf = ctypes.create_string_buffer(blob, len(blob))
+        with _DeviceGuard(self.device):
+            call("awqb_tp_exchange_open", self._ctx, buf)
+
+    def gemm_allreduce(self, x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
+                       bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y[..., N] = sum over ranks of x_r[..., K] @ dequant(blob_r) (+ bias), on every rank."""
+        from ..ops import _check_cuda, _dtype_code, gemm_workspace_bytes, workspace_pool
+
+        if x.shape[-1] != K:
+            raise ValueError(f"x has {x.shape[-1]} features, expected K={K}")
+        x2 = x.reshape(-1, K)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        M = x2.shape[0]
+        if M > self.max_rows or N > self.max_n:
+            raise ValueError(f"exchange sized for M <= {self.max_rows}, N <= {self.max_n}")
+        code = _dtype_code(x.dtype)
+        dev = _check_cuda(x2, blob)
+        if bias is not None and (bias.dtype != x.dtype or bias.numel() != N):
+            raise ValueError("bias must be [N] in the activation dtype")
+        if out is None:
+            out = torch.empty((M, N), dtype=x.dtype, device=dev)
+        elif out.numel() != M * N or out.dtype != x.dtype or not out.is_contiguous():
+            raise ValueError("out must be a contiguous [M, N] tensor of the activation dtype")
+        if M == 0:
+            return out.reshape(*x.shape[:-1], N)
+        ws = workspace_pool.get(dev, gemm_workspace_bytes(M, K, N, G))
+        with _DeviceGuard(dev):
+            call("awqb_gemm_allreduce", _p(x2), M, K, N, G, code, _p(blob), _p(bias), _p(out), _p(ws),
+                 ws.numel(), self._ctx, _stream(dev))
+        return out.reshape(*x.shape[:-1], N)
+
+    def destroy(self) -> None:
+        if self._ctx.value:
+            with _DeviceGuard(self.device):
+                call("awqb_tp_exchange_destroy", self._ctx)
+            self._ctx = ctypes.c_void_p(0)
+
+
+def init_peer_exchange(*, tp_rank: int, tp_size: int, tp_cpu_group, device: torch.device,
+                       max_rows: int = 64, max_n: int = 8192) -> PeerExchange:
+    """Create the exchange on every rank and map the peers' buffers (handles
+    travel over the CPU group)."""
+    import torch.distributed as dist
+
+    ex = PeerExchange(tp_rank, tp_size, device, max_rows, max_n)
+    handles = [None] * tp_size
+    if tp_size > 1:
+        dist.all_gather_object(handles, ex.handle(), group=tp_cpu_group)
+    else:
+        handles = [ex.handle()]
+    ex.open(handles)
+    return ex
+
+
+__all__ = ["NcclCommunicator", "PeerExchange", "get_unique_id", "init_nccl", "init_peer_exchange"]

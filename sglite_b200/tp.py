@@ -84,14 +84,31 @@ class ColumnParallelAWQLinear(_AWQLinear):
 
 
 class RowParallelAWQLinear(_AWQLinear):
-    """O / down: input features split across ranks, output all-reduced."""
+    """O / down: input features split across ranks, output all-reduced
+    (``RowParallelLinear.forward``, layers/linear.py:189-194).
 
-    def __init__(self, method, input_size: int, output_size: int, tp_size: int, comm=None, bias=None):
+    With a ``PeerExchange`` and no bias, decode-sized batches (M <= its
+    max_rows) run the GEMM fused with the all-reduce in one kernel over peer
+    memory; otherwise the GEMM is followed by the NCCL all-reduce. (The
+    reference adds the bias on every rank before reducing; that case keeps the
+    NCCL path so the semantics stay identical.)"""
+
+    def __init__(self, method, input_size: int, output_size: int, tp_size: int, comm=None, bias=None,
+                 exchange=None):
         super().__init__(method, div_even(input_size, tp_size), output_size, bias)
         self.tp_size = tp_size
         self.comm = comm
+        self.exchange = exchange
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.tp_size > 1 and self.exchange is not None and self.bias is None:
+            M = x.numel() // self.local_input_size
+            if M <= self.exchange.max_rows and self.local_output_size <= self.exchange.max_n:
+                w = self.weights
+                if x.dtype != w["_act_dtype"]:
+                    raise ValueError(f"activations are {x.dtype}, weights were loaded for {w['_act_dtype']}")
+                return self.exchange.gemm_allreduce(x, w["qweight"], self.local_input_size,
+                                                    self.local_output_size, w["_group_size"])
         y = super().forward(x)
         if self.tp_size > 1:
             y = self.comm.all_reduce(y)

@@ -25,7 +25,7 @@ def _worker(rank, world, port, q):
     from datetime import timedelta
 
     from oracle.awq_ref import awq_linear_ref, rel_err
-    from sglite_b200.distributed import init_nccl
+    from sglite_b200.distributed import init_nccl, init_peer_exchange
     from sglite_b200.quantization import AWQB200Config
     from sglite_b200.synthetic import make_activations, make_awq_weights
     from sglite_b200.tp import ColumnParallelAWQLinear, RowParallelAWQLinear, shard_awq
@@ -35,10 +35,12 @@ def _worker(rank, world, port, q):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
-    comm = None
+    comm = ex = None
     try:
         comm = init_nccl(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
                          max_size_bytes=64 * 4096 * 2)
+        ex = init_peer_exchange(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
+                                max_rows=64, max_n=4096)
         method = AWQB200Config(4, 128, True).get_linear_method()
         G, K, N = 128, 4096, 4096
         dt = torch.bfloat16
@@ -47,6 +49,8 @@ def _worker(rank, world, port, q):
         row.load({k: v.to(dev) for k, v in shard_awq(full, "row", rank, world).items()})
         col = ColumnParallelAWQLinear(method, K, N // world)
         col.load({k: v.to(dev) for k, v in shard_awq(full, "column", rank, world).items()})
+        rowf = RowParallelAWQLinear(method, K, N, world, comm, exchange=ex)
+        rowf.load({k: v.to(dev) for k, v in shard_awq(full, "row", rank, world).items()})
         for M in (1, 64, 700):  # 700 x 4096 x 2 B exceeds the symmetric window: in-place path
             x = make_activations(M, K, dt, seed=M)
             xl = x[:, rank * K // world:(rank + 1) * K // world].contiguous().to(dev)
@@ -54,14 +58,26 @@ def _worker(rank, world, port, q):
             ref = awq_linear_ref(x, full["qweight"], full["qzeros"], full["scales"], G)
             e = rel_err(y, ref)
             assert e <= 1e-2, (M, e)
+            # fused GEMM + all-reduce over peer memory (M <= 64; NCCL above)
+            for _ in range(3):
+                yf = rowf.forward(xl)
+                assert rel_err(yf, ref) <= 1e-2, (M, rel_err(yf, ref))
+            # every rank holds the same bits
+            got = [None] * world
+            dist.all_gather_object(got, yf.float().cpu().numpy().tobytes())
+            assert all(g == got[0] for g in got)
             yc = col.forward(x.to(dev))
             refc = ref[:, rank * N // world:(rank + 1) * N // world]
             assert rel_err(yc, refc) <= 1e-2
         torch.cuda.synchronize()
+        from sglite_b200 import ops
+        assert ops.device_error() == 0
         q.put((rank, "ok"))
-    except Exception as ex:
-        q.put((rank, repr(ex)))
+    except Exception as err:
+        q.put((rank, repr(err)))
     finally:
+        if ex is not None:
+            ex.destroy()
         if comm is not None:
             comm.destroy()
         dist.destroy_process_group()
