@@ -131,7 +131,7 @@ struct GemmCfg {
   static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK + (kATmem ? kSD * kAStageCols : 0)));
   static_assert(kSD >= 2, "need two A stages");
   static_assert(kTmemCols <= 512, "TMEM over capacity");
-  static_assert((2 * kSL + 2 * kSD + 6) * 8 + 32 <= 512, "barrier area overflow");
+  static_assert((3 * kSL + 2 * kSD + 6) * 8 + 32 <= 512, "barrier area overflow");
   static_assert(kSL >= 2, "not enough shared memory for two load stages");
   static_assert(kSmemBytes <= 232448, "shared memory over the sm_100 per-CTA limit");
   static_assert(NTOK % 16 == 0 && NTOK >= 16 && NTOK <= 256, "MMA N must be 16..256 step 16");
@@ -332,9 +332,10 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   uint8_t* lring = base;
   uint8_t* wring = base + SL * Cfg::kLStage;
   uint64_t* bars = reinterpret_cast<uint64_t*>(wring + SD * Cfg::kWStage);
-  uint64_t* full_l = bars;             // [SL]  TMA bytes landed
-  uint64_t* empty_l = bars + SL;       // [SL]  dequant warps + MMA done with the stage
-  uint64_t* full_d = bars + 2 * SL;    // [SD]  dequantised A stage written
+  uint64_t* full_w = bars;             // [SL]  the stage's packed weights landed
+  uint64_t* full_x = bars + SL;        // [SL]  the stage's activations landed
+  uint64_t* empty_l = bars + 2 * SL;   // [SL]  dequant warps + MMA done with the stage
+  uint64_t* full_d = bars + 3 * SL;    // [SD]  dequantised A stage written
   uint64_t* empty_d = full_d + SD;     // [SD]  MMA done reading the A stage
   uint64_t* acc_full = empty_d + SD;   // [2]
   uint64_t* acc_empty = acc_full + 2;  // [2]
@@ -362,7 +363,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < SL; ++i) {
-      mbar_init(smem_u32(&full_l[i]), 1);
+      mbar_init(smem_u32(&full_w[i]), 1);
+      mbar_init(smem_u32(&full_x[i]), 1);
       mbar_init(smem_u32(&empty_l[i]), Cfg::kDqPerStage + 1);
     }
     for (int i = 0; i < SD; ++i) {
@@ -421,8 +423,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const uint8_t* blob = p.blob;
     int blob_mt = -1;
     // Weights do not depend on the previous kernel in the stream: the first
-    // stages' weight copies go out before waiting for it, their activations
-    // after (each stage's barrier expects both).
+    // stages' weight copies go out before waiting for it (and are dequantised
+    // as they land, on their own barrier), their activations after.
     const int early = cmin(SL, n_local);
     {
       WorkPos ue = up;
@@ -432,9 +434,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           break;
         }
         const uint8_t* src = blob + ((int64_t)ue.nt * KB + ue.kb * SB) * Cfg::kPkBytes;
-        const uint32_t bar = smem_u32(&full_l[j]);
+        const uint32_t bar = smem_u32(&full_w[j]);
         if (elect_one()) {
-          mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
+          mbar_arrive_expect_tx(bar, Cfg::kPkStage);
           bulk_g2s(smem_u32(lring + j * Cfg::kLStage), src, Cfg::kPkStage, bar, pol_w);
         }
         __syncwarp();
@@ -457,13 +459,15 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       }
       const uint8_t* src = blob + ((int64_t)up.nt * KB + up.kb * SB) * Cfg::kPkBytes;
       uint8_t* stg = lring + st.idx * Cfg::kLStage;
-      const uint32_t bar = smem_u32(&full_l[st.idx]);
+      const uint32_t bar = smem_u32(&full_x[st.idx]);
       const bool weights_sent = weights_early && issued < early;
       if (elect_one()) {
         if (!weights_sent) {
-          mbar_arrive_expect_tx(bar, Cfg::kPkStage + Cfg::kXBytes);
-          bulk_g2s(smem_u32(stg), src, Cfg::kPkStage, bar, pol_w);
+          const uint32_t wbar = smem_u32(&full_w[st.idx]);
+          mbar_arrive_expect_tx(wbar, Cfg::kPkStage);
+          bulk_g2s(smem_u32(stg), src, Cfg::kPkStage, wbar, pol_w);
         }
+        mbar_arrive_expect_tx(bar, Cfg::kXBytes);
         if (p.x3d) {
           tma_load_3d(smem_u32(stg + Cfg::kPkRegion), &tmap_x, 0, up.mt * NTOK, up.kb * Cfg::kXAtoms, bar,
                       pol_x);
@@ -483,7 +487,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     for (int j = 0; j < cmin(issued, SL); ++j) {
       if (st.idx == 0) st.phase ^= 1u;
       st.idx = (st.idx == 0 ? SL : st.idx) - 1;
-      if (!mbar_wait(smem_u32(&full_l[st.idx]), st.phase)) {
+      if (!mbar_wait(smem_u32(&full_w[st.idx]), st.phase) || !mbar_wait(smem_u32(&full_x[st.idx]), st.phase)) {
         if (lane == 0) atomicOr(p.err, kErrWaitDrain);
         break;
       }
@@ -512,7 +516,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)(acc.idx * NTOK);
       for (; u < seg_end; ++u) {
-        if (!mbar_wait(smem_u32(&full_l[sl.idx]), sl.phase) ||
+        if (!mbar_wait(smem_u32(&full_x[sl.idx]), sl.phase) ||
             !mbar_wait(smem_u32(&full_d[sd.idx]), sd.phase)) {
           if (lane == 0) atomicOr(p.err, kErrWaitMma);
           *s_abort = 1;
@@ -906,7 +910,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     int il = dg % SL, pl = (dg >= SL);    // load-ring slot / phase of this group's current stage
     int id = dg % SD, pd = (dg >= SD);    // A-ring slot / phase
     for (int u = dg; u < n_local; u += 2) {
-      if (!mbar_wait(smem_u32(&full_l[il]), (uint32_t)pl)) {
+      if (!mbar_wait(smem_u32(&full_w[il]), (uint32_t)pl)) {
         atomicOr(p.err, kErrWaitDequant);
         *s_abort = 1;
         break;
