@@ -422,26 +422,14 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     int issued = 0;
     const uint8_t* blob = p.blob;
     int blob_mt = -1;
-    // Weights do not depend on the previous kernel in the stream: the first
-    // stages' weight copies go out before waiting for it (and are dequantised
-    // as they land, on their own barrier), their activations after.
+    // Weights do not depend on the previous kernel in the stream: the epilogue
+    // warps (idle until the first accumulator) copy the first `early` stages'
+    // weights before the grid dependency resolves, and the dequantisers start on
+    // them as they land (own barrier). The producer only adds the activations of
+    // those stages, after the wait. Each bulk copy takes ~0.3 us to issue, so
+    // spreading them over four warps gets the producer to its first activation
+    // load sooner.
     const int early = cmin(SL, n_local);
-    {
-      WorkPos ue = up;
-      for (int j = 0; j < early; ++j, ue.next(sch)) {
-        if (p.tile_expert != nullptr) {
-          // expert ids are written by the routing kernel: wait before reading them
-          break;
-        }
-        const uint8_t* src = blob + ((int64_t)ue.nt * KB + ue.kb * SB) * Cfg::kPkBytes;
-        const uint32_t bar = smem_u32(&full_w[j]);
-        if (elect_one()) {
-          mbar_arrive_expect_tx(bar, Cfg::kPkStage);
-          bulk_g2s(smem_u32(lring + j * Cfg::kLStage), src, Cfg::kPkStage, bar, pol_w);
-        }
-        __syncwarp();
-      }
-    }
     const bool weights_early = (p.tile_expert == nullptr);
     grid_dep_wait();
     for (; up.j < n_local; up.next(sch)) {
@@ -567,6 +555,23 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const int f = q * 32 + lane;            // feature row within the tile
     const int etid = threadIdx.x - Cfg::kEpiWarp0 * 32;
     constexpr int kEpiThreads = Cfg::kNumEpiWarps * 32;
+    if (p.tile_expert == nullptr && n_local > 0) {
+      // early weight copies (see the producer); expert ids of the grouped GEMM
+      // come from the previous kernel, so those wait for the producer's loop
+      const uint64_t pol_w = MT > 1 ? policy_evict_normal() : policy_evict_first();
+      const int early = cmin(SL, n_local);
+      for (int j = warp - Cfg::kEpiWarp0; j < early; j += Cfg::kNumEpiWarps) {
+        WorkPos ue;
+        ue.init(j, sch);
+        const uint8_t* src = p.blob + ((int64_t)ue.nt * KB + ue.kb * SB) * Cfg::kPkBytes;
+        const uint32_t bar = smem_u32(&full_w[j]);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(bar, Cfg::kPkStage);
+          bulk_g2s(smem_u32(lring + j * Cfg::kLStage), src, Cfg::kPkStage, bar, pol_w);
+        }
+        __syncwarp();
+      }
+    }
     grid_dep_wait();  // outputs, workspace counters and partials belong to the previous grid until then
     if (etid == 0) *s_tpe = p.tp_world > 0 ? (uint32_t)*reinterpret_cast<volatile int*>(p.tp_epoch) : 0u;
     named_bar_sync(1, kEpiThreads);
