@@ -612,6 +612,22 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK);
       };
 
+      // Scattered output (MoE): the destination row and scale of the first 16
+      // rows do not depend on the accumulator; fetch them before waiting for it.
+      int pf_m = 0;
+      float pf_s = 1.f;
+      bool pf_ok = false;
+      if (p.row_map != nullptr || p.row_scale != nullptr) {
+        const int li = lane & 15;
+        pf_m = mt * NTOK + li;
+        pf_ok = li < rows_here;
+        if (pf_ok && p.row_map != nullptr) {
+          pf_m = p.row_map[pf_m];
+          pf_ok = pf_m < p.num_valid;
+        }
+        if (pf_ok && p.row_scale != nullptr) pf_s = p.row_scale[pf_m];
+      }
+
       // Wait for the accumulator. Meanwhile an owner whose peers have all
       // published sums their partials (in contributor order) into the spare TMEM
       // buffer, so the fix-up costs nothing once its own MMAs are done; it gives
@@ -695,14 +711,19 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           return;
         }
         const int li = lane & 15;
-        int my_m = mt * NTOK + c0 + li;
-        float my_s = 1.f;
-        bool my_ok = li < cnt && c0 + li < rows_here;
-        if (my_ok && p.row_map != nullptr) {
-          my_m = p.row_map[my_m];
-          my_ok = my_m < p.num_valid;
+        int my_m = pf_m;
+        float my_s = pf_s;
+        bool my_ok = pf_ok && li < cnt;
+        if (c0 != 0) {
+          my_m = mt * NTOK + c0 + li;
+          my_s = 1.f;
+          my_ok = li < cnt && c0 + li < rows_here;
+          if (my_ok && p.row_map != nullptr) {
+            my_m = p.row_map[my_m];
+            my_ok = my_m < p.num_valid;
+          }
+          if (my_ok && p.row_scale != nullptr) my_s = p.row_scale[my_m];
         }
-        if (my_ok && p.row_scale != nullptr) my_s = p.row_scale[my_m];
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           if (c >= cnt) break;
