@@ -598,13 +598,13 @@ def run_moe(args):
     E, k, H, I = 128, 8, 2048, 768
     g = torch.Generator(device=dev).manual_seed(0)
 
-    def experts(K, N):
+    def experts(K, N, gate_up=False):
         qw = torch.randint(-2**31, 2**31 - 1, (E, K, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
         qz = torch.randint(-2**31, 2**31 - 1, (E, K // G, N // 8), generator=g, device=dev, dtype=torch.int64).to(torch.int32)
         sc = (torch.rand((E, K // G, N), generator=g, device=dev) * 9e-3 + 1e-3).to(DTYPE)
-        return AWQExpertWeights.from_awq(qw, qz, sc, G)
+        return AWQExpertWeights.from_awq(qw, qz, sc, G, gate_up=gate_up)
 
-    w1, w2 = experts(H, 2 * I), experts(I, H)
+    w1, w2 = experts(H, 2 * I, gate_up=True), experts(I, H)
     backend = AWQB200MoeBackend()
     hbm, tflops_peak, kind = _peaks()
     per = {}

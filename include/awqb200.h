@@ -143,11 +143,33 @@ int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int64_t K, int
                           const int32_t* row_map, const float* row_scale, int64_t num_valid,
                           void* y, int64_t ldy, void* workspace, int64_t workspace_bytes,
                           void* stream);
+/* The gate_up projection fused with SiLU-and-mul: y[M][N/2] = silu(x W_gate) *
+ * (x W_up), computed from the fp32 accumulators (one rounding). The blob must
+ * come from AWQ tensors whose columns are interleaved one by one (column 2j =
+ * gate j, column 2j + 1 = up j; ops.interleave_gate_up repacks the AWQ
+ * tensors). N % 16 == 0; bias (if any) is interleaved the same way. Replaces the gate_up GEMM + SiluAndMul pair of the MLP
+ * (layers/activation.py:11-22, blocks.py:53-57) and of the MoE experts
+ * (fused.py:160-178). Workspace as for awqb_gemm. */
+int awqb_gemm_silu_mul(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                       const void* blob, const void* bias, void* y, void* workspace,
+                       int64_t workspace_bytes, void* stream);
+/* The same for the MoE expert gate_up GEMM over expert-sorted rows: y [rows][ldy]
+ * with ldy >= N / 2, rows in sorted order (as awqb_moe_grouped_gemm without
+ * row_map / row_scale). */
+int awqb_moe_grouped_gemm_silu_mul(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
+                                   int64_t G, int dtype, const void* blobs, int64_t blob_stride,
+                                   const int32_t* block_expert, const int32_t* num_post_pad, int ntok,
+                                   void* y, int64_t ldy, void* workspace, int64_t workspace_bytes,
+                                   void* stream);
 /* out[r][j] = silu(in[r][j]) * in[r][I + j] in fp32; rows = min(rows_max,
  * *rows_dev) when rows_dev is given. Replaces silu_and_mul (flashinfer),
  * srt/model_executor/layers/activation.py:11-15. */
 int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
                       int dtype, void* out, void* stream);
+/* The same for gate_up outputs in the interleaved layout of awqb_gemm_silu_mul
+ * (in[r][2j] = gate j, in[r][2j + 1] = up j). */
+int awqb_silu_and_mul_interleaved(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
+                                  int dtype, void* out, void* stream);
 /* out[m][h] = sum_k in[m][k][h] (fp32 accumulate), counting only pairs whose
  * expert is in [e_begin, e_end) when topk_ids is given.
  * Replaces moe_sum_reduce_triton, kernels/moe_triton.py:68-102. */

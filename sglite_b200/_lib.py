@@ -45,12 +45,17 @@ _SIGNATURES = {
     "awqb_moe_align": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp]),
     "awqb_moe_gather_rows": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "awqb_moe_grouped_workspace_bytes": (c_int, [c_i64, c_i64, c_i64, c_i64, c_int, c_i64p]),
+    "awqb_gemm_silu_mul": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "awqb_moe_grouped_gemm_silu_mul": (
+        c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_i64, c_vp, c_vp, c_int, c_vp, c_i64, c_vp, c_i64,
+                c_vp]),
     "awqb_moe_grouped_gemm": (
         c_int,
         [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_i64, c_vp, c_vp, c_int, c_vp, c_vp, c_i64,
          c_vp, c_i64, c_vp, c_i64, c_vp],
     ),
     "awqb_silu_and_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp]),
+    "awqb_silu_and_mul_interleaved": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp]),
     "awqb_moe_topk_sum": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_int, c_vp, c_vp]),
     "awqb_nccl_unique_id_bytes": (c_int, []),
     "awqb_nccl_get_unique_id": (c_int, [c_vp]),

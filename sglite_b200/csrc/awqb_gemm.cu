@@ -322,11 +322,14 @@ struct TpExchange {
 int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
               const void* blob, const void* bias, void* y, void* workspace,
               int64_t workspace_bytes, int ntok, int64_t ctas, void* stream,
-              const TpExchange* tp = nullptr) {
+              const TpExchange* tp = nullptr, bool silu = false) {
   AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
                "dtype %d is not fp16 (0) or bf16 (1)", dtype);
+  AWQB_REQUIRE(!silu || N % 16 == 0, kInvalidArgument,
+               "fused SiLU-and-mul needs N = 2 * intermediate with intermediate a multiple of 8 (N=%lld)",
+               (long long)N);
   Plan pl;
-  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true, tp != nullptr);
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, !silu, tp != nullptr);
   if (st != kOk) return st;
   if (M == 0) return kOk;
   AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
@@ -349,7 +352,8 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.blob = static_cast<const uint8_t*>(blob);
   p.bias = bias;
   p.y = y;
-  p.ldy = N;
+  p.ldy = silu ? N / 2 : N;
+  p.silu_mul = silu ? 1 : 0;
   p.num_valid = 0;
   p.M = (int32_t)M;
   p.N = (int32_t)N;
@@ -385,10 +389,13 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
 
 using namespace awqb;
 
+// Workspace sizes are those of the stream-K plan, which covers every launch the
+// same arguments can make (cluster split-K needs no partials; fused SiLU-and-mul
+// and the fused all-reduce use the same or a cluster plan).
 extern "C" int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_t G,
                                          int64_t* bytes) {
   Plan pl;
-  int st = make_plan(M, K, N, G, 0, 0, &pl, true);
+  int st = make_plan(M, K, N, G, 0, 0, &pl, false);
   if (st != kOk) return st;
   AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
   *bytes = pl.cnt_bytes + pl.part_bytes;
@@ -398,7 +405,7 @@ extern "C" int awqb_gemm_workspace_bytes(int64_t M, int64_t K, int64_t N, int64_
 extern "C" int awqb_gemm_workspace_bytes_ex(int64_t M, int64_t K, int64_t N, int64_t G, int ntok,
                                             int64_t ctas, int64_t* bytes) {
   Plan pl;
-  int st = make_plan(M, K, N, G, ntok, ctas, &pl, true);
+  int st = make_plan(M, K, N, G, ntok, ctas, &pl, false);
   if (st != kOk) return st;
   AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
   *bytes = pl.cnt_bytes + pl.part_bytes;
@@ -416,6 +423,13 @@ extern "C" int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int nt
   *ctas_out = pl.ctas;
   *cluster_out = pl.cluster_s;
   return kOk;
+}
+
+extern "C" int awqb_gemm_silu_mul(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                                  const void* blob, const void* bias, void* y, void* workspace,
+                                  int64_t workspace_bytes, void* stream) {
+  return awqb::gemm_impl(x, M, K, N, G, dtype, blob, bias, y, workspace, workspace_bytes, 0, 0, stream, nullptr,
+                         true);
 }
 
 extern "C" int awqb_gemm(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
@@ -531,12 +545,14 @@ extern "C" int awqb_moe_grouped_workspace_bytes(int64_t rows_max, int64_t K, int
   return kOk;
 }
 
-extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
+namespace awqb {
+namespace {
+int grouped_impl(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
                                      int64_t G, int dtype, const void* blobs, int64_t blob_stride,
                                      const int32_t* block_expert, const int32_t* num_post_pad,
                                      int ntok, const int32_t* row_map, const float* row_scale,
                                      int64_t num_valid, void* y, int64_t ldy, void* workspace,
-                                     int64_t workspace_bytes, void* stream) {
+                                     int64_t workspace_bytes, void* stream, bool silu) {
   AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
                "dtype %d is not fp16 (0) or bf16 (1)", dtype);
   AWQB_REQUIRE(ntok == 16 || ntok == 32 || ntok == 64 || ntok == 128 || ntok == 256,
@@ -552,7 +568,7 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   AWQB_REQUIRE(x_sorted && blobs && block_expert && num_post_pad && y, kInvalidArgument, "null pointer");
   AWQB_REQUIRE(((uintptr_t)x_sorted & 15) == 0 && ((uintptr_t)blobs & 15) == 0 && blob_stride % 16 == 0,
                kInvalidArgument, "x_sorted, blobs and blob_stride must be 16-byte aligned");
-  AWQB_REQUIRE(ldy >= N, kInvalidArgument, "ldy < N");
+  AWQB_REQUIRE(ldy >= (silu ? N / 2 : N), kInvalidArgument, "ldy too small");
   AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
                "workspace must be non-null and 256-byte aligned");
   AWQB_REQUIRE(workspace_bytes >= pl.cnt_bytes + pl.part_bytes, kInvalidArgument,
@@ -571,6 +587,7 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   p.rows_valid = num_post_pad;
   p.y = y;
   p.ldy = ldy;
+  p.silu_mul = silu ? 1 : 0;
   p.row_map = row_map;
   p.row_scale = row_scale;
   p.num_valid = (int32_t)num_valid;
@@ -588,6 +605,31 @@ extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, false, s);
   return launch_n<__nv_bfloat16>(tm, p, pl, false, s);
+}
+}  // namespace
+}  // namespace awqb
+
+extern "C" int awqb_moe_grouped_gemm(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
+                                     int64_t G, int dtype, const void* blobs, int64_t blob_stride,
+                                     const int32_t* block_expert, const int32_t* num_post_pad,
+                                     int ntok, const int32_t* row_map, const float* row_scale,
+                                     int64_t num_valid, void* y, int64_t ldy, void* workspace,
+                                     int64_t workspace_bytes, void* stream) {
+  return awqb::grouped_impl(x_sorted, rows_max, K, N, G, dtype, blobs, blob_stride, block_expert, num_post_pad,
+                            ntok, row_map, row_scale, num_valid, y, ldy, workspace, workspace_bytes, stream, false);
+}
+
+extern "C" int awqb_moe_grouped_gemm_silu_mul(const void* x_sorted, int64_t rows_max, int64_t K, int64_t N,
+                                              int64_t G, int dtype, const void* blobs, int64_t blob_stride,
+                                              const int32_t* block_expert, const int32_t* num_post_pad,
+                                              int ntok, void* y, int64_t ldy, void* workspace,
+                                              int64_t workspace_bytes, void* stream) {
+  using namespace awqb;
+  AWQB_REQUIRE(N % 16 == 0, kInvalidArgument, "fused SiLU-and-mul needs N a multiple of 16 (N=%lld)",
+               (long long)N);
+  AWQB_REQUIRE(ldy >= N / 2, kInvalidArgument, "ldy < N / 2");
+  return grouped_impl(x_sorted, rows_max, K, N, G, dtype, blobs, blob_stride, block_expert, num_post_pad, ntok,
+                      nullptr, nullptr, 0, y, ldy, workspace, workspace_bytes, stream, true);
 }
 
 // ---------------------------------------------------------------------------

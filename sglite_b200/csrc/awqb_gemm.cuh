@@ -85,6 +85,8 @@ struct GemmParams {
                                 //   each CTA owns; zero between calls
   uint32_t* err;                // device error word
   int32_t x3d;                  // X tensor map is 3-D {64, rows, K/64}: one load per stage
+  int32_t silu_mul;             // columns interleaved gate j, up j: the output is
+                                //   silu(gate) * up, N / 2 features, dense rows
   int32_t group_m;              // token tiles per raster group (>= 1)
   int32_t cluster_s;            // >= 2: launched in clusters of cluster_s CTAs, one tile per
                                 //   cluster; its partials are reduced through DSMEM
@@ -690,6 +692,26 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       // each (row_map) and its scale (row_scale) are read once per chunk by
       // lanes 0..15 and broadcast with shuffles (warp-uniform loop).
       auto store_row_vals = [&](int c0, const float* vals, int cnt) {
+        if (p.silu_mul) {
+          // Column 2j is gate j, column 2j + 1 is up j: the pair sits in
+          // neighbouring lanes. One shuffle swaps them; the gate lane writes the
+          // even token columns, the up lane the odd ones.
+          const int odd = f & 1;
+          const int no = n >> 1;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c >= cnt) break;
+            const float mine = vals[c] + bias_v;
+            const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            if ((c & 1) == odd && c0 + c < rows_here && n < p.N) {
+              const float g = odd ? other : mine;
+              const float u = odd ? mine : other;
+              reinterpret_cast<T*>(p.y)[(int64_t)(mt * NTOK + c0 + c) * p.ldy + no] =
+                  (T)(__fdividef(g, 1.f + __expf(-g)) * u);
+            }
+          }
+          return;
+        }
         if (p.tp_world > 0) {  // fused all-reduce: tagged words to every rank's landing slot (no bias yet)
           if (n >= p.N) return;
           const uint32_t e = *s_tpe;

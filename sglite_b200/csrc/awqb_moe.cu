@@ -187,7 +187,7 @@ __device__ __forceinline__ float to_f(T v) { return (float)v; }
 
 // out[r, j] = silu(in[r, j]) * in[r, I + j], computed in fp32; eight
 // elements (16 bytes) per thread and iteration (I % 8 == 0).
-template <typename T>
+template <typename T, bool kInterleaved>
 __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
                                     const int32_t* __restrict__ rows_dev, int I, T* __restrict__ out) {
   int64_t rows = rows_max;
@@ -197,16 +197,29 @@ __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
        t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = t / iv;
     const int j = (int)(t - r * iv) * 8;
-    const uint4 gv = *reinterpret_cast<const uint4*>(in + r * 2 * I + j);
-    const uint4 uv = *reinterpret_cast<const uint4*>(in + r * 2 * I + I + j);
-    const T* g = reinterpret_cast<const T*>(&gv);
-    const T* u = reinterpret_cast<const T*>(&uv);
     uint4 ov;
     T* o = reinterpret_cast<T*>(&ov);
+    if constexpr (kInterleaved) {  // columns 2j = gate j, 2j + 1 = up j
+      const uint4 a = *reinterpret_cast<const uint4*>(in + r * 2 * I + 2 * j);
+      const uint4 b = *reinterpret_cast<const uint4*>(in + r * 2 * I + 2 * j + 8);
+      const T* pa = reinterpret_cast<const T*>(&a);
+      const T* pb = reinterpret_cast<const T*>(&b);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float gf = to_f(g[i]);
-      o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(u[i]));
+      for (int i = 0; i < 8; ++i) {
+        const T* pr = i < 4 ? pa + 2 * i : pb + 2 * (i - 4);
+        const float gf = to_f(pr[0]);
+        o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(pr[1]));
+      }
+    } else {
+      const uint4 gv = *reinterpret_cast<const uint4*>(in + r * 2 * I + j);
+      const uint4 uv = *reinterpret_cast<const uint4*>(in + r * 2 * I + I + j);
+      const T* g = reinterpret_cast<const T*>(&gv);
+      const T* u = reinterpret_cast<const T*>(&uv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float gf = to_f(g[i]);
+        o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(u[i]));
+      }
     }
     *reinterpret_cast<uint4*>(out + r * I + j) = ov;
   }
@@ -314,8 +327,9 @@ extern "C" int awqb_moe_gather_rows(const void* x, int64_t K, const int32_t* sor
   return kOk;
 }
 
-extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
-                                 int dtype, void* out, void* stream) {
+namespace {
+int silu_and_mul_impl(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I, int dtype, void* out,
+                      void* stream, bool interleaved) {
   AWQB_REQUIRE(I > 0 && I % 8 == 0 && rows_max >= 0, kInvalidArgument, "I=%lld must be a positive multiple of 8",
                (long long)I);
   AWQB_REQUIRE(((uintptr_t)in & 15) == 0 && ((uintptr_t)out & 15) == 0, kInvalidArgument,
@@ -324,17 +338,29 @@ extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t
   if (rows_max == 0) return kOk;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned g = grid1d(rows_max * (I / 8), 256);
-  if (dtype == AWQB_DTYPE_F16)
-    silu_and_mul_kernel<__half><<<g, 256, 0, s>>>(static_cast<const __half*>(in), rows_max, rows_dev,
-                                                   (int)I, static_cast<__half*>(out));
-  else if (dtype == AWQB_DTYPE_BF16)
-    silu_and_mul_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), rows_max,
-                                                          rows_dev, (int)I,
-                                                          static_cast<__nv_bfloat16*>(out));
-  else
+  if (dtype == AWQB_DTYPE_F16) {
+    auto k = interleaved ? silu_and_mul_kernel<__half, true> : silu_and_mul_kernel<__half, false>;
+    k<<<g, 256, 0, s>>>(static_cast<const __half*>(in), rows_max, rows_dev, (int)I, static_cast<__half*>(out));
+  } else if (dtype == AWQB_DTYPE_BF16) {
+    auto k = interleaved ? silu_and_mul_kernel<__nv_bfloat16, true> : silu_and_mul_kernel<__nv_bfloat16, false>;
+    k<<<g, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(in), rows_max, rows_dev, (int)I,
+                        static_cast<__nv_bfloat16*>(out));
+  } else {
     AWQB_REQUIRE(false, kInvalidArgument, "bad dtype %d", dtype);
+  }
   AWQB_LAUNCH_CHECK();
   return kOk;
+}
+}  // namespace
+
+extern "C" int awqb_silu_and_mul(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
+                                 int dtype, void* out, void* stream) {
+  return silu_and_mul_impl(in, rows_max, rows_dev, I, dtype, out, stream, false);
+}
+
+extern "C" int awqb_silu_and_mul_interleaved(const void* in, int64_t rows_max, const int32_t* rows_dev, int64_t I,
+                                             int dtype, void* out, void* stream) {
+  return silu_and_mul_impl(in, rows_max, rows_dev, I, dtype, out, stream, true);
 }
 
 extern "C" int awqb_moe_topk_sum(const void* in, int64_t M, int64_t topk, int64_t H,

@@ -46,6 +46,7 @@ class AWQExpertWeights:
     act_dtype: torch.dtype
     e_begin: int = 0             # first global expert id held here
     num_global_experts: Optional[int] = None
+    gate_up_interleaved: bool = False  # w1 columns interleaved gate j, up j (fused SiLU-and-mul)
 
     @property
     def num_experts(self) -> int:
@@ -57,12 +58,20 @@ class AWQExpertWeights:
 
     @classmethod
     def from_awq(cls, qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor, group_size: int,
-                 e_begin: int = 0, num_global_experts: Optional[int] = None) -> "AWQExpertWeights":
-        """qweight [E, K, N/8] int32, qzeros [E, K/G, N/8] int32, scales [E, K/G, N] (device tensors)."""
+                 e_begin: int = 0, num_global_experts: Optional[int] = None,
+                 gate_up: bool = False) -> "AWQExpertWeights":
+        """qweight [E, K, N/8] int32, qzeros [E, K/G, N/8] int32, scales [E, K/G, N] (device tensors).
+        gate_up=True for the merged gate_up projection (w1): its columns are
+        interleaved at load so the GEMM can apply SiLU-and-mul in its epilogue
+        (needs the intermediate size to be a multiple of 8; otherwise the plain
+        layout is kept and SiLU-and-mul runs as its own kernel)."""
         E, K, N8 = qweight.shape
         G = K if group_size == -1 else group_size
+        inter = gate_up and (N8 * 8) % 16 == 0
+        if inter:
+            qweight, qzeros, scales = ops.interleave_gate_up(qweight, qzeros, scales)
         blob = ops.repack(qweight.contiguous(), qzeros.contiguous(), scales.contiguous(), G)
-        return cls(blob, K, N8 * 8, G, scales.dtype, e_begin, num_global_experts)
+        return cls(blob, K, N8 * 8, G, scales.dtype, e_begin, num_global_experts, inter)
 
 
 def choose_block_m(num_tokens: int, topk: int, num_experts: int) -> int:
@@ -107,9 +116,15 @@ class AWQB200MoeBackend(BaseMoeBackend):
         sorted_ids, block_expert, npp = ops.moe_align(topk_ids, w1.e_begin, w1.e_end, block_m)
         rows = sorted_ids.numel()
         xs = ops.moe_gather_rows(x, sorted_ids, npp, topk, numel)
-        h1 = torch.empty((rows, w1.N), dtype=x.dtype, device=x.device)
-        ops.moe_grouped_gemm(xs, w1.blob, w1.K, w1.N, w1.G, block_expert, npp, block_m, h1)
-        a = ops.silu_and_mul(h1, rows_dev=npp)
+        if w1.gate_up_interleaved and block_m <= 64:
+            # gate_up GEMM with SiLU-and-mul in its epilogue (measured faster up to
+            # 64-row expert blocks; above, the separate kernel wins)
+            a = torch.empty((rows, w1.N // 2), dtype=x.dtype, device=x.device)
+            ops.moe_grouped_gemm_silu_mul(xs, w1.blob, w1.K, w1.N, w1.G, block_expert, npp, block_m, a)
+        else:
+            h1 = torch.empty((rows, w1.N), dtype=x.dtype, device=x.device)
+            ops.moe_grouped_gemm(xs, w1.blob, w1.K, w1.N, w1.G, block_expert, npp, block_m, h1)
+            a = ops.silu_and_mul(h1, rows_dev=npp, interleaved=w1.gate_up_interleaved)
         y3 = torch.empty((numel, H), dtype=x.dtype, device=x.device)
         ops.moe_grouped_gemm(a, w2.blob, w2.K, w2.N, w2.G, block_expert, npp, block_m, y3,
                              row_map=sorted_ids, row_scale=topk_weights.reshape(-1).contiguous(), num_valid=numel)

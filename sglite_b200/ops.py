@@ -320,16 +320,92 @@ def moe_grouped_gemm(x_sorted: torch.Tensor, blobs: torch.Tensor, K: int, N: int
     return out
 
 
+_AWQ_SHIFT = (0, 16, 4, 20, 8, 24, 12, 28)  # bit offset of logical column i of a packed word
+
+
+def _awq_unpack_cols(w: torch.Tensor) -> torch.Tensor:
+    """[..., C/8] int32 in AWQ order -> [..., C] uint8 nibbles."""
+    sh = torch.tensor(_AWQ_SHIFT, dtype=torch.int32, device=w.device)
+    return ((w.unsqueeze(-1) >> sh) & 0xF).to(torch.uint8).reshape(*w.shape[:-1], w.shape[-1] * 8)
+
+
+def _awq_pack_cols(q: torch.Tensor) -> torch.Tensor:
+    """[..., C] nibbles -> [..., C/8] int32 in AWQ order."""
+    sh = torch.tensor(_AWQ_SHIFT, dtype=torch.int64, device=q.device)
+    w = (q.reshape(*q.shape[:-1], q.shape[-1] // 8, 8).to(torch.int64) << sh).sum(-1)
+    return torch.where(w >= 2**31, w - 2**32, w).to(torch.int32)
+
+
+def interleave_gate_up(qweight: torch.Tensor, qzeros: torch.Tensor, scales: torch.Tensor,
+                       bias: Optional[torch.Tensor] = None):
+    """Reorder merged gate_up AWQ tensors ([..., K, 2I/8] packed, [..., K/G, 2I]
+    scales) so that column 2j is gate column j and column 2j + 1 is up column j
+    (the layout of gemm_silu_mul). Nibbles are moved, never changed: the
+    dequantised weights are a column permutation of the originals."""
+    two_i = scales.shape[-1]
+    if two_i % 16 != 0:
+        raise ValueError("fused SiLU-and-mul needs the intermediate size to be a multiple of 8")
+    I = two_i // 2
+    j = torch.arange(I, device=scales.device)
+    cols = torch.stack([j, I + j], dim=1).reshape(-1)
+    qw = _awq_pack_cols(_awq_unpack_cols(qweight).index_select(-1, cols.to(qweight.device)))
+    qz = _awq_pack_cols(_awq_unpack_cols(qzeros).index_select(-1, cols.to(qzeros.device)))
+    out = (qw.contiguous(), qz.contiguous(), scales.index_select(-1, cols).contiguous())
+    if bias is not None:
+        return out + (bias.index_select(-1, cols.to(bias.device)).contiguous(),)
+    return out
+
+
+def gemm_silu_mul(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
+                  bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """silu(x @ W_gate) * (x @ W_up) -> [..., N/2] from an interleaved gate_up blob."""
+    if x.shape[-1] != K:
+        raise ValueError(f"x has {x.shape[-1]} features, expected K={K}")
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    code = _dtype_code(x.dtype)
+    dev = _check_cuda(x2, blob)
+    if out is None:
+        out = torch.empty((M, N // 2), dtype=x.dtype, device=dev)
+    elif out.numel() != M * (N // 2) or out.dtype != x.dtype or not out.is_contiguous():
+        raise ValueError("out must be a contiguous [M, N/2] tensor of the activation dtype")
+    if M == 0:
+        return out.reshape(*x.shape[:-1], N // 2)
+    ws = workspace_pool.get(dev, gemm_workspace_bytes(M, K, N, G))
+    with _DeviceGuard(dev):
+        call("awqb_gemm_silu_mul", _p(x2), M, K, N, G, code, _p(blob), _p(bias), _p(out), _p(ws), ws.numel(),
+             _stream(dev))
+    return out.reshape(*x.shape[:-1], N // 2)
+
+
+def moe_grouped_gemm_silu_mul(x_sorted: torch.Tensor, blobs: torch.Tensor, K: int, N: int, G: int,
+                              block_expert: torch.Tensor, num_post_pad: torch.Tensor, block_m: int,
+                              out: torch.Tensor) -> torch.Tensor:
+    """Expert gate_up GEMM fused with SiLU-and-mul (interleaved w1): out [rows, N/2]."""
+    dev = _check_cuda(x_sorted, blobs, block_expert, num_post_pad, out)
+    rows = x_sorted.shape[0]
+    nb = c_i64(0)
+    call("awqb_moe_grouped_workspace_bytes", rows, K, N, G, block_m, ctypes.byref(nb))
+    ws = workspace_pool.get(dev, nb.value)
+    with _DeviceGuard(dev):
+        call("awqb_moe_grouped_gemm_silu_mul", _p(x_sorted), rows, K, N, G, _dtype_code(x_sorted.dtype),
+             _p(blobs), blobs.stride(0), _p(block_expert), _p(num_post_pad), block_m, _p(out), out.shape[-1],
+             _p(ws), ws.numel(), _stream(dev))
+    return out
+
+
 def silu_and_mul(h: torch.Tensor, rows_dev: Optional[torch.Tensor] = None,
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """silu(h[:, :I]) * h[:, I:] in fp32, rounded to h's dtype."""
+                 out: Optional[torch.Tensor] = None, interleaved: bool = False) -> torch.Tensor:
+    """silu(h[:, :I]) * h[:, I:] in fp32, rounded to h's dtype (interleaved:
+    silu(h[:, 0::2]) * h[:, 1::2], the layout of an interleaved gate_up)."""
     dev = _check_cuda(h)
     rows, two_i = h.shape
     I = two_i // 2
     if out is None:
         out = torch.empty((rows, I), dtype=h.dtype, device=dev)
     with _DeviceGuard(dev):
-        call("awqb_silu_and_mul", _p(h), rows, _p(rows_dev), I, _dtype_code(h.dtype), _p(out), _stream(dev))
+        call("awqb_silu_and_mul_interleaved" if interleaved else "awqb_silu_and_mul", _p(h), rows, _p(rows_dev), I,
+             _dtype_code(h.dtype), _p(out), _stream(dev))
     return out
 
 

@@ -116,3 +116,20 @@ def test_process_weights_requires_cuda_and_apply_requires_processing():
         m.process_weights_after_loading(w)
     with pytest.raises(RuntimeError):
         m.apply_weights(w, torch.zeros(1, 256))
+
+
+def test_interleave_gate_up_is_a_column_permutation():
+    """Interleaving moves nibbles, never changes them: column 2j of the result
+    dequantises to gate column j, column 2j + 1 to up column j."""
+    import torch
+    from oracle.awq_ref import dequant_ref
+    from sglite_b200 import ops
+    from sglite_b200.synthetic import make_awq_weights
+
+    K, I, G = 256, 192, 128
+    w = make_awq_weights(K, 2 * I, G, torch.float16, seed=3)
+    qw, qz, sc = ops.interleave_gate_up(w["qweight"], w["qzeros"], w["scales"])
+    Wi = dequant_ref(qw, qz, sc, G)
+    W = dequant_ref(w["qweight"], w["qzeros"], w["scales"], G)
+    cols = [c for j in range(I) for c in (j, I + j)]
+    assert torch.equal(Wi, W[:, cols])

@@ -167,3 +167,25 @@ def test_gemm_cluster_split_k(cuda, K, N, M):
     assert rel_err(y, y_sk.float()) <= TOL
     assert torch.equal(y, ops.gemm(x.to(cuda), blob, K, N, G))  # deterministic
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("I", [64, 200, 768])
+@pytest.mark.parametrize("M", [1, 5, 64, 300])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_silu_mul_fused(cuda, I, M, dtype):
+    """gate_up GEMM with SiLU-and-mul in the epilogue (columns interleaved at
+    load) against the oracle: silu(x W_gate) * (x W_up) in fp32."""
+    from oracle.awq_ref import dequant_ref
+
+    K, G = 512, 128
+    w = make_awq_weights(K, 2 * I, G, dtype, seed=I + M)
+    x = make_activations(M, K, dtype, seed=M)
+    qw, qz, sc = ops.interleave_gate_up(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")))
+    blob = ops.repack(qw, qz, sc, G)
+    y = ops.gemm_silu_mul(x.to(cuda), blob, K, 2 * I, G)
+    W = dequant_ref(w["qweight"], w["qzeros"], w["scales"], G).float()
+    h = x.float() @ W
+    ref = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
+    assert y.shape == (M, I)
+    assert rel_err(y, ref) <= TOL
+    assert ops.device_error() == 0

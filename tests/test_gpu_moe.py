@@ -39,19 +39,22 @@ def test_align_matches_oracle_exactly(cuda, M, E, k, bm, ep):
     assert (sorted_ids[n:] == ids.numel()).all()  # unused tail carries the sentinel
 
 
-def _experts(E, H, I, G, dtype, seed, cuda):
+def _experts(E, H, I, G, dtype, seed, cuda, fused=True):
     w1 = make_awq_weights(H, 2 * I, G, dtype, seed=seed, batch=E)
     w2 = make_awq_weights(I, H, G, dtype, seed=seed + 1, batch=E)
-    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G, gate_up=fused)
     e2 = AWQExpertWeights.from_awq(*(w2[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    assert e1.gate_up_interleaved == fused
     return w1, w2, e1, e2
 
 
 @pytest.mark.parametrize("M", [1, 7, 64, 300])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_moe_pipeline_matches_oracle(cuda, M, dtype):
+@pytest.mark.parametrize("fused", [False, True])
+def test_moe_pipeline_matches_oracle(cuda, M, dtype, fused):
+    """fused: SiLU-and-mul inside the gate_up GEMM's epilogue (interleaved w1)."""
     E, k, H, I, G = 16, 4, 256, 128, 128
-    w1, w2, e1, e2 = _experts(E, H, I, G, dtype, 11, cuda)
+    w1, w2, e1, e2 = _experts(E, H, I, G, dtype, 11, cuda, fused)
     x = make_activations(M, H, dtype, seed=M)
     lg = make_router_logits(M, E, seed=M + 1)
     y = AWQB200MoeBackend().forward(x.to(cuda).clone(), e1, e2, lg.to(cuda), k, True)
@@ -85,7 +88,7 @@ def test_moe_matches_reference_kernels_golden(cuda, golden):
     w2 = {k: torch.from_numpy(golden["moe_w2_" + k]) for k in ("qweight", "qzeros", "scales")}
     w1["scales"] = w1["scales"].view(torch.float16)
     w2["scales"] = w2["scales"].view(torch.float16)
-    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    e1 = AWQExpertWeights.from_awq(*(w1[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G, gate_up=True)
     e2 = AWQExpertWeights.from_awq(*(w2[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
     x = torch.from_numpy(golden["moe_x"]).view(torch.float16)
     lg = torch.from_numpy(golden["moe_logits"])
@@ -105,3 +108,14 @@ def test_qwen3_30b_a3b_moe_shape(cuda, M):
     ref = moe_ref(x, w1, w2, lg, k, True, G)
     assert rel_err(y, ref.float()) <= TOL
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("interleaved", [False, True])
+def test_silu_and_mul_layouts(cuda, interleaved):
+    from oracle.awq_ref import silu_and_mul_ref
+
+    rows, I = 37, 136
+    h = torch.randn(rows, 2 * I, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    plain = torch.cat([h[:, 0::2], h[:, 1::2]], dim=1) if interleaved else h
+    out = ops.silu_and_mul(h.to(cuda), interleaved=interleaved)
+    assert torch.allclose(out.float().cpu(), silu_and_mul_ref(plain).float(), rtol=1e-2, atol=1e-2)
