@@ -116,9 +116,9 @@ class AWQB200MoeBackend(BaseMoeBackend):
         sorted_ids, block_expert, npp = ops.moe_align(topk_ids, w1.e_begin, w1.e_end, block_m)
         rows = sorted_ids.numel()
         xs = ops.moe_gather_rows(x, sorted_ids, npp, topk, numel)
-        if w1.gate_up_interleaved and block_m <= 64:
-            # gate_up GEMM with SiLU-and-mul in its epilogue (measured faster up to
-            # 64-row expert blocks; above, the separate kernel wins)
+        if w1.gate_up_interleaved and block_m <= ops.SILU_FUSE_MAX_M:
+            # gate_up GEMM with SiLU-and-mul in its epilogue (measured faster for
+            # small expert blocks; above, the separate kernel wins)
             a = torch.empty((rows, w1.N // 2), dtype=x.dtype, device=x.device)
             ops.moe_grouped_gemm_silu_mul(xs, w1.blob, w1.K, w1.N, w1.G, block_expert, npp, block_m, a)
         else:
