@@ -235,6 +235,7 @@ def run_ours(args):
         if args.allreduce == "fused":
             ex = init_peer_exchange(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
                                     max_rows=max(MS), max_n=4096)
+            ex.set_mode(args.tp_mode)
 
     cfg = AWQB200Config(4, G, True)
     method = cfg.get_linear_method()
@@ -543,6 +544,7 @@ def run_tp70b(args):
         if args.allreduce == "fused":
             ex = init_peer_exchange(tp_rank=rank, tp_size=world, tp_cpu_group=dist.group.WORLD, device=dev,
                                     max_rows=64, max_n=8192)
+            ex.set_mode(args.tp_mode)
     full = {"qkv": (8192, 10240), "o": (8192, 8192), "gate_up": (8192, 57344), "down": (28672, 8192)}
     loc = {n: ((K // world, N) if n in ROW_PARALLEL else (K, N // world)) for n, (K, N) in full.items()}
     ws = {}
@@ -579,8 +581,8 @@ def run_tp70b(args):
         print(json.dumps({"workload": f"llama3.1_70b_awq_layer_tp{world} (config 3)", "metric": "TP-layer us",
                           "unit": "us", "n_gpus": world, "per_m": out,
                           "roofline": "max(weight bytes / measured HBM, flops / measured bf16 peak) + 2 ring all-reduces at 770 GB/s",
-                          "allreduce": ("fused GEMM + all-reduce over peer memory for M <= 64, NCCL above"
-                                        if ex is not None else "NCCL"),
+                          "allreduce": (f"fused GEMM + all-reduce over peer memory for M <= 64 ({args.tp_mode}), "
+                                        "NCCL above" if ex is not None else "NCCL"),
                           "peak_kind": kind}), flush=True)
     if ex is not None:
         ex.destroy()
@@ -634,6 +636,8 @@ def main():
                     help="decode (default, the contract line) or another BASELINE config")
     ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
                     help="row-parallel all-reduce at N > 1: fused into the GEMM over peer memory, or NCCL")
+    ap.add_argument("--tp-mode", default="auto", choices=["auto", "all_to_all", "reduce_scatter"],
+                    help="exchange pattern of the fused all-reduce")
     ap.add_argument("--shape", default="4096x28672x1", help="KxNxM for --workload gemm")
     ap.add_argument("--fp16", action="store_true", help="fp16 activations for --workload gemm")
     args = ap.parse_args()

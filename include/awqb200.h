@@ -204,7 +204,7 @@ int awqb_nccl_destroy(void* comm);
  *
  * Set-up, once per rank of the group (collective in spirit: every rank must do
  * it): awqb_tp_exchange_create allocates this rank's exchange buffer
- * (cudaMalloc, 16 * world * max_rows * max_n bytes + 256) on the current
+ * (cudaMalloc, (16 * world + 8) * max_rows * max_n bytes + 256) on the current
  * device; exchange the awqb_tp_exchange_handle bytes of all ranks (any host
  * channel), then awqb_tp_exchange_open(ctx, handles of ranks 0..world-1 back to
  * back). Every rank must then issue the same sequence of awqb_gemm_allreduce
@@ -217,6 +217,15 @@ int awqb_tp_exchange_handle_bytes(int64_t* bytes);
 int awqb_tp_exchange_create(int rank, int world, int64_t max_rows, int64_t max_n, void** ctx);
 int awqb_tp_exchange_handle(void* ctx, void* handle_out);
 int awqb_tp_exchange_open(void* ctx, const void* handles);
+/* Exchange pattern of the fused all-reduce (every rank must set the same):
+ * 0 auto (reduce-scatter + all-gather from 4 ranks and 8 rows, on launches
+ * that split K over a thread-block cluster; all-to-all otherwise), 1 always
+ * all-to-all (each rank sends its partial to every rank; every rank sums),
+ * 2 reduce-scatter + all-gather wherever the launch allows it (each rank sends
+ * its partial of feature tile t to rank t % world only; that rank sums and
+ * sends the rounded result to the others). Results are bit-identical across
+ * modes: every sum is taken in rank order. No counterpart in the reference. */
+int awqb_tp_exchange_set_mode(void* ctx, int mode);
 int awqb_tp_exchange_destroy(void* ctx);
 int awqb_gemm_allreduce(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
                         const void* blob, const void* bias, void* y, void* workspace,

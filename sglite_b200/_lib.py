@@ -67,6 +67,7 @@ _SIGNATURES = {
     "awqb_tp_exchange_create": (c_int, [c_int, c_int, c_i64, c_i64, ctypes.POINTER(c_vp)]),
     "awqb_tp_exchange_handle": (c_int, [c_vp, c_vp]),
     "awqb_tp_exchange_open": (c_int, [c_vp, c_vp]),
+    "awqb_tp_exchange_set_mode": (c_int, [c_vp, c_int]),
     "awqb_tp_exchange_destroy": (c_int, [c_vp]),
     "awqb_gemm_allreduce": (
         c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_vp]),

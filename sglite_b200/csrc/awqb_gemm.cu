@@ -310,13 +310,21 @@ struct TpExchange {
   int rank = 0, world = 1, device = 0;
   int64_t rows = 0, max_n = 0;
   int64_t half_words = 0;    // landing words per parity
+  int64_t final_half = 0;    // final words (reduce-scatter mode) per parity
+  int mode = 0;              // 0 auto, 1 all-to-all, 2 reduce-scatter + all-gather
   void* local = nullptr;     // this rank's allocation
   void* base[8] = {};        // every rank's allocation as mapped here
   bool opened = false;
   int64_t land_bytes() const { return 2 * half_words * 8; }
-  int64_t total_bytes() const { return land_bytes() + 256; }
+  int64_t final_bytes() const { return 2 * final_half * 4; }
+  int64_t total_bytes() const { return land_bytes() + final_bytes() + 256; }
   uint2* land(int r) const { return static_cast<uint2*>(base[r]); }
-  int32_t* epoch() const { return reinterpret_cast<int32_t*>(static_cast<uint8_t*>(local) + land_bytes()); }
+  uint32_t* final_words(int r) const {
+    return reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(base[r]) + land_bytes());
+  }
+  int32_t* epoch() const {
+    return reinterpret_cast<int32_t*>(static_cast<uint8_t*>(local) + land_bytes() + final_bytes());
+  }
 };
 
 int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
@@ -376,8 +384,17 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
     p.tp_rank = tp->rank;
     p.tp_rows = (int32_t)tp->rows;
     p.tp_half = tp->half_words;
-    for (int r = 0; r < tp->world; ++r) p.tp_land[r] = tp->land(r);
+    p.tp_fhalf = tp->final_half;
+    for (int r = 0; r < tp->world; ++r) {
+      p.tp_land[r] = tp->land(r);
+      p.tp_final[r] = tp->final_words(r);
+    }
     p.tp_epoch = tp->epoch();
+    // Reduce-scatter + all-gather once the all-to-all traffic (world x the
+    // result, in 8-byte words) outweighs the extra hop: from 4 ranks and 8
+    // rows; implemented in the cluster split-K finale.
+    const bool rsag = tp->mode == 2 || (tp->mode == 0 && tp->world >= 4 && M >= 8);
+    p.tp_rsag = (pl.cluster_s > 1 && rsag) ? 1 : 0;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);
@@ -647,6 +664,7 @@ extern "C" int awqb_tp_exchange_create(int rank, int world, int64_t max_rows, in
   t->rows = max_rows;
   t->max_n = max_n;
   t->half_words = (int64_t)world * max_rows * max_n;
+  t->final_half = max_rows * max_n;
   cudaError_t e = cudaGetDevice(&t->device);
   if (e == cudaSuccess) e = cudaMalloc(&t->local, (size_t)t->total_bytes());
   if (e == cudaSuccess) e = cudaMemset(t->local, 0, (size_t)t->total_bytes());
@@ -696,6 +714,14 @@ extern "C" int awqb_tp_exchange_handle_bytes(int64_t* bytes) {
   using namespace awqb;
   AWQB_REQUIRE(bytes != nullptr, kInvalidArgument, "bytes is null");
   *bytes = (int64_t)sizeof(cudaIpcMemHandle_t);
+  return kOk;
+}
+
+extern "C" int awqb_tp_exchange_set_mode(void* ctx, int mode) {
+  using namespace awqb;
+  AWQB_REQUIRE(ctx != nullptr, kInvalidArgument, "ctx is null");
+  AWQB_REQUIRE(mode >= 0 && mode <= 2, kInvalidArgument, "mode must be 0 (auto), 1 or 2");
+  static_cast<TpExchange*>(ctx)->mode = mode;
   return kOk;
 }
 

@@ -100,6 +100,12 @@ struct GemmParams {
   uint2* tp_land[8];            // per rank (peer-mapped): landing words, [2][world][rows][N]
   int32_t* tp_epoch;            // this rank's call counter (tag = epoch + 1, buffer = epoch & 1)
                                 //   and the count of CTAs done with the call
+  // Reduce-scatter + all-gather mode (tp_rsag): the values of feature tile nt
+  // go only to rank nt % world, which sums them, stores them and sends the
+  // final values ({16-bit value, 16-bit tag} words) to the other ranks.
+  int32_t tp_rsag;
+  uint32_t* tp_final[8];        // per rank (peer-mapped): final words, [2][rows][N]
+  int64_t tp_fhalf;             // final words per parity half
 };
 
 template <int NTOK, int GPB>
@@ -274,6 +280,75 @@ __device__ __forceinline__ float silu_fast(float g) {
 // buffer (out of line: keeps the epilogue's registers free).
 __device__ __noinline__ void tp_put(uint2* const* lands, int world, int64_t off, float v, uint32_t tag) {
   for (int d = 0; d < world; ++d) st_tagged_sys(lands[d] + off, v, tag);
+}
+
+// Tag of the final words: 15 bits of the call counter, never 0 (a zeroed buffer
+// never matches).
+__device__ __forceinline__ uint32_t tp_tag16(uint32_t epoch) { return (epoch & 0x7fffu) + 1u; }
+
+// Fused all-reduce at the end of a cluster split-K tile: this CTA's slice,
+// features n0 .. n0+nf-1 of rows m0 .. m0+rows-1, was sent to the landing
+// buffers. Wait for the tagged words, then store (sum of every rank's partial
+// in rank order, or, in the reduce-scatter mode on a rank that does not own the
+// tile, the owner's final values; the owner sends those). Out of line: runs
+// once per CTA.
+template <typename T>
+__device__ __noinline__ void tp_cluster_finish(const GemmParams& p, int n0, int nf, int m0, int rows,
+                                               uint32_t epoch) {
+  const int par = (int)(epoch & 1u);
+  const uint32_t tag = epoch + 1u;
+  const uint32_t t16 = tp_tag16(epoch);
+  const bool recv = p.tp_rsag && (n0 / kBlockN) % p.tp_world != p.tp_rank;
+  const uint2* land = p.tp_land[p.tp_rank] + (int64_t)par * p.tp_half;
+  const uint32_t* fin = p.tp_final[p.tp_rank] + (int64_t)par * p.tp_fhalf;
+  uint64_t t0 = 0;
+  for (int e = threadIdx.x; e < nf * rows; e += blockDim.x) {
+    const int c = e / nf;
+    const int n = n0 + (e - c * nf);
+    if (n >= p.N) continue;
+    const int m = m0 + c;
+    T out;
+    if (recv) {
+      const uint32_t* wp = fin + (int64_t)m * p.N + n;
+      uint32_t w = ld_word_sys(wp);
+      while ((w >> 16) != t16) {
+        if (t0 == 0) {
+          t0 = globaltimer_ns();
+        } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+          atomicOr(p.err, 8u);  // kErrWaitEpilogue
+          return;
+        }
+        w = ld_word_sys(wp);
+      }
+      const uint16_t b = (uint16_t)(w & 0xffffu);
+      out = *reinterpret_cast<const T*>(&b);
+    } else {
+      float v = 0.f;
+      for (int r = 0; r < p.tp_world; ++r) {
+        const uint2* wp = land + ((int64_t)r * p.tp_rows + m) * p.N + n;
+        uint2 w = ld_tagged_sys(wp);
+        while (w.y != tag) {
+          if (t0 == 0) {
+            t0 = globaltimer_ns();
+          } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+            atomicOr(p.err, 8u);
+            return;
+          }
+          w = ld_tagged_sys(wp);
+        }
+        v += __uint_as_float(w.x);
+      }
+      if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
+      out = (T)v;
+      if (p.tp_rsag) {
+        const uint32_t w = (uint32_t) * reinterpret_cast<const uint16_t*>(&out) | (t16 << 16);
+        const int64_t fo = (int64_t)par * p.tp_fhalf + (int64_t)m * p.N + n;
+        for (int d = 0; d < p.tp_world; ++d)
+          if (d != p.tp_rank) st_word_sys(p.tp_final[d] + fo, w);
+      }
+    }
+    reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = out;
+  }
 }
 
 // Fused all-reduce, final step for one feature column of a tile: wait until
@@ -770,6 +845,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       // Fused all-reduce, after this thread has written its final values of the
       // tile to every rank: wait for each rank's word of each of its values
       // (tag of this call), sum them in rank order, add the bias, store.
+      // (The reduce-scatter mode is only used with cluster split-K plans; the
+      // stream-K path always exchanges all-to-all.)
       auto tp_finish = [&]() {
         if (n >= p.N) return;
         const uint32_t e = *s_tpe;
@@ -1071,47 +1148,19 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       const int n = nt * kBlockN + f;
       if (n < p.N) {
         const int m = mt * NTOK + c;
-        if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's landing slot
+        if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's (or the owner's) landing slot
           const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
-          for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tp_tag);
+          if (p.tp_rsag)
+            st_tagged_sys(p.tp_land[nt % p.tp_world] + o, v, tp_tag);
+          else
+            for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tp_tag);
         } else {
           if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
           reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)v;
         }
       }
     }
-    if (p.tp_world > 0) {
-      // Each thread waits for every rank's word of the values it contributed,
-      // then sums them in rank order.
-      const uint2* land = p.tp_land[p.tp_rank] + (int64_t)tp_par * p.tp_half;
-      uint64_t t0 = 0;
-      bool ok = true;
-      for (int e = threadIdx.x; e < nf * rows_here && ok; e += Cfg::kThreads) {
-        const int c = e / nf;
-        const int n = nt * kBlockN + f0 + (e - c * nf);
-        if (n >= p.N) continue;
-        const int m = mt * NTOK + c;
-        float v = 0.f;
-        for (int r = 0; r < p.tp_world && ok; ++r) {
-          const uint2* wp = land + ((int64_t)r * p.tp_rows + m) * p.N + n;
-          uint2 w = ld_tagged_sys(wp);
-          while (w.y != tp_tag) {
-            if (t0 == 0) t0 = globaltimer_ns();
-            else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
-              atomicOr(p.err, kErrWaitEpilogue);
-              ok = false;
-              break;
-            }
-            w = ld_tagged_sys(wp);
-          }
-          v += __uint_as_float(w.x);
-        }
-        if (ok) {
-          if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
-          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)v;
-        }
-      }
-    }
+    if (p.tp_world > 0) tp_cluster_finish<T>(p, nt * kBlockN + f0, nf, mt * NTOK, rows_here, tp_epoch);
     cluster_sync_all();
   }
   if (p.tp_world > 0 && threadIdx.x == 0) {

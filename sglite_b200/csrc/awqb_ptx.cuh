@@ -351,6 +351,16 @@ __device__ __forceinline__ uint2 ld_tagged_sys(const void* addr) {
   return r;
 }
 
+// 4-byte {16-bit value, 16-bit tag} words (the all-gather of final values).
+__device__ __forceinline__ void st_word_sys(void* addr, uint32_t w) {
+  asm volatile("st.relaxed.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(w) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_word_sys(const void* addr) {
+  uint32_t r;
+  asm volatile("ld.relaxed.sys.global.b32 %0, [%1];" : "=r"(r) : "l"(addr) : "memory");
+  return r;
+}
+
 // Acquire fence (gpu scope) for the thread that observed the final count.
 __device__ __forceinline__ void fence_acquire_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");

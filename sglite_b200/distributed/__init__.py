@@ -121,6 +121,15 @@ class PeerExchange:
         with _DeviceGuard(self.device):
             call("awqb_tp_exchange_open", self._ctx, buf)
 
+    MODES = {"auto": 0, "all_to_all": 1, "reduce_scatter": 2}
+
+    def set_mode(self, mode: str) -> None:
+        """Exchange pattern: "auto", "all_to_all" or "reduce_scatter" (same on
+        every rank; results are bit-identical across patterns)."""
+        if mode not in self.MODES:
+            raise ValueError(f"mode must be one of {sorted(self.MODES)}")
+        call("awqb_tp_exchange_set_mode", self._ctx, self.MODES[mode])
+
     def gemm_allreduce(self, x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
                        bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """y[..., N] = sum over ranks of x_r[..., K] @ dequant(blob_r) (+ bias), on every rank."""

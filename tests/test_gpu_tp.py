@@ -58,10 +58,16 @@ def _worker(rank, world, port, q):
             ref = awq_linear_ref(x, full["qweight"], full["qzeros"], full["scales"], G)
             e = rel_err(y, ref)
             assert e <= 1e-2, (M, e)
-            # fused GEMM + all-reduce over peer memory (M <= 64; NCCL above)
-            for _ in range(3):
-                yf = rowf.forward(xl)
-                assert rel_err(yf, ref) <= 1e-2, (M, rel_err(yf, ref))
+            # fused GEMM + all-reduce over peer memory (M <= 64; NCCL above),
+            # all-to-all and reduce-scatter + all-gather: identical bits
+            yfs = []
+            for mode in ("all_to_all", "reduce_scatter", "auto"):
+                ex.set_mode(mode)
+                for _ in range(3):
+                    yf = rowf.forward(xl)
+                    assert rel_err(yf, ref) <= 1e-2, (M, mode, rel_err(yf, ref))
+                yfs.append(yf.clone())
+            assert all(torch.equal(yfs[0], t) for t in yfs), M
             # every rank holds the same bits
             got = [None] * world
             dist.all_gather_object(got, yf.float().cpu().numpy().tobytes())

@@ -26,9 +26,11 @@ def _blob(cuda, K, N, G, dt, seed):
     return w, ops.repack(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
 
 
+@pytest.mark.parametrize("mode", ["auto", "reduce_scatter"])
 @pytest.mark.parametrize("K,N", [(4096, 4096), (1024, 8192), (3584, 8192), (2048, 1000)])
-def test_fused_equals_plain_gemm(cuda, exchange, K, N):
+def test_fused_equals_plain_gemm(cuda, exchange, K, N, mode):
     G, dt = 128, torch.bfloat16
+    exchange.set_mode(mode)
     w, blob = _blob(cuda, K, N, G, dt, K + N)
     for rep in range(3):  # consecutive calls alternate the landing / flag parity
         for M in (1, 5, 33, 64):
