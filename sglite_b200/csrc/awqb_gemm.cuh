@@ -1116,14 +1116,16 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     }
   }
 
+  __syncwarp();  // roles end after per-lane waits: reconverge before the aligned barrier
   __syncthreads();
   if (p.cluster_s > 1) {
     // Cluster split-K finale: every CTA of the cluster holds a partial of the
     // same tile in shared memory ([row][128 features] fp32). Rank r sums the
-    // features [128 r / S, 128 (r+1) / S) over the S partials in rank order
-    // (deterministic), reading its peers' shared memory directly, and stores
-    // them; the second barrier keeps every CTA's shared memory alive until its
-    // peers have read it.
+    // features of its slice, whole 16-byte quads [4 (32 r / S), 4 (32 (r+1) / S)),
+    // over the S partials in rank order (deterministic), reading its peers'
+    // shared memory directly (one 16-byte load per peer and quad), and stores
+    // them. It then signals that it is done reading its peers; the final wait
+    // keeps its own shared memory alive until they are done reading it.
     cluster_sync_all();
     const int S = p.cluster_s;
     const int rank = (int)cluster_ctarank();
@@ -1131,37 +1133,49 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     int mt, nt;
     sch.tile_mn(tile, mt, nt);
     const int rows_here = n_local > 0 ? cmax(0, cmin(NTOK, p.M - mt * NTOK)) : 0;
-    const int f0 = rank * 128 / S;
-    const int nf = (rank + 1) * 128 / S - f0;
+    const int f0 = 4 * (rank * 32 / S);
+    const int nf = 4 * ((rank + 1) * 32 / S) - f0;
+    const int nq = nf >> 2;
     const uint32_t tp_epoch = p.tp_world > 0 ? (uint32_t)*reinterpret_cast<volatile int*>(p.tp_epoch) : 0u;
     const int tp_par = (int)(tp_epoch & 1u);
     const uint32_t tp_tag = tp_epoch + 1u;
     const uint32_t base_sm = smem_u32(lring);
-    for (int e = threadIdx.x; e < nf * rows_here; e += Cfg::kThreads) {
-      const int c = e / nf;
-      const int f = f0 + (e - c * nf);
+    for (int e = threadIdx.x; e < nq * rows_here; e += Cfg::kThreads) {
+      const int c = e / nq;
+      const int f = f0 + 4 * (e - c * nq);
       const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
-      float v = 0.f;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int r = 0; r < 8; ++r)
-        if (r < S) v += ld_dsmem_f32(mapa_shared(off, (uint32_t)r));
-      const int n = nt * kBlockN + f;
-      if (n < p.N) {
-        const int m = mt * NTOK + c;
+      for (int r = 0; r < 8; ++r) {
+        if (r < S) {
+          const float4 a = ld_dsmem_v4(mapa_shared(off, (uint32_t)r));
+          v[0] += a.x;
+          v[1] += a.y;
+          v[2] += a.z;
+          v[3] += a.w;
+        }
+      }
+      const int m = mt * NTOK + c;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = nt * kBlockN + f + j;
+        if (n >= p.N) break;
         if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's (or the owner's) landing slot
           const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
           if (p.tp_rsag)
-            st_tagged_sys(p.tp_land[nt % p.tp_world] + o, v, tp_tag);
+            st_tagged_sys(p.tp_land[nt % p.tp_world] + o, v[j], tp_tag);
           else
-            for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tp_tag);
+            for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v[j], tp_tag);
         } else {
-          if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
-          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)v;
+          float out = v[j];
+          if (p.bias != nullptr) out += (float)reinterpret_cast<const T*>(p.bias)[n];
+          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)out;
         }
       }
     }
+    cluster_arrive();
     if (p.tp_world > 0) tp_cluster_finish<T>(p, nt * kBlockN + f0, nf, mt * NTOK, rows_here, tp_epoch);
-    cluster_sync_all();
+    cluster_wait();
   }
   if (p.tp_world > 0 && threadIdx.x == 0) {
     // The last CTA to finish advances this rank's call counter (the parity of

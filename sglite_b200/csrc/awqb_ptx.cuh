@@ -263,8 +263,12 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8])
                : "memory");
 }
 // AND-reduction of a predicate over the threads of a named barrier.
+// Aligned barriers count a warp once per arrival: a warp that reaches one
+// diverged (lanes leaving a per-lane spin-wait at different times) would be
+// counted twice, so every helper reconverges the warp first.
 __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
   uint32_t r;
+  __syncwarp();
   asm volatile(
       "{\n\t.reg .pred p, q;\n\t"
       "setp.ne.u32 p, %1, 0;\n\t"
@@ -374,13 +378,31 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
 }
 // All threads of all CTAs of the cluster; release / acquire at cluster scope.
 __device__ __forceinline__ void cluster_sync_all() {
+  __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync_all, for work in between.
+__device__ __forceinline__ void cluster_arrive() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  __syncwarp();
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Shared-memory address of the same variable in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
+}
+__device__ __forceinline__ float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
   float v;
@@ -395,6 +417,7 @@ __device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.w
 __device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  __syncwarp();
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 

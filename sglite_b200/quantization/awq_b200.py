@@ -155,11 +155,13 @@ class AWQB200LinearMethod(LinearMethodBase):
         }
 
     def apply_weights(self, weights: Dict[str, Any], x: torch.Tensor,
-                      bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      bias: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if not weights.get("_weights_processed", False):
             raise RuntimeError("process_weights_after_loading must run before apply_weights")
         if x.dtype != weights["_act_dtype"]:
             raise ValueError(f"activation dtype {x.dtype} differs from the scales dtype "
                              f"{weights['_act_dtype']} the weights were loaded with")
+        # out: optional preallocated [..., N] result (e.g. a slice of a buffer the
+        # caller copies to the host in one piece)
         return ops.gemm(x, weights["qweight"], weights["_input_size"], weights["_output_size"],
-                        weights["_group_size"], bias=bias)
+                        weights["_group_size"], bias=bias, out=out)
