@@ -714,11 +714,15 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         if (pf_ok && p.row_scale != nullptr) pf_s = p.row_scale[pf_m];
       }
 
-      // Wait for the accumulator. Meanwhile an owner whose peers have all
-      // published sums their partials (in contributor order) into the spare TMEM
-      // buffer, so the fix-up costs nothing once its own MMAs are done; it gives
-      // up as soon as its accumulator is ready (the reducer path then runs).
+      // Wait for the accumulator. Meanwhile an owner checks whether its peers
+      // have all published. Up to 16 rows it then sums their partials (in
+      // contributor order) into the spare TMEM buffer, so the fix-up costs
+      // nothing once its own MMAs are done; it gives up as soon as its
+      // accumulator is ready. With more rows that sum would take several round
+      // trips to L2: the owner instead reduces as soon as its accumulator is
+      // ready, without an arrival ticket (it knows it is the last to arrive).
       bool pre = false;
+      bool published = false;
       {
         const uint32_t bar = smem_u32(&acc_full[acc.idx]);
         bool done = mbar_try_wait(bar, acc.phase);
@@ -729,9 +733,10 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
             // every lane acquires for itself; the decision is warp-uniform
             if (__all_sync(0xffffffffu, ld_acquire_gpu(&cnt[1]) == ncontrib - 1)) {
               tried = true;
-              bool complete = true;
+              published = true;
+              bool complete = rows_here <= 16;
 #pragma unroll 1
-              for (int c0 = 0; c0 < rows_here; c0 += 8) {
+              for (int c0 = 0; complete && c0 < rows_here; c0 += 8) {
                 if (c0 > 0 && mbar_test_wait(bar, acc.phase)) {
                   complete = false;
                   done = true;
@@ -755,7 +760,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
                 tmem_st8(t_spare + (uint32_t)c0, sv);
               }
               tmem_st_wait();
-              pre = complete;
+              pre = complete && rows_here <= 16;
               if (done) break;
             }
           }
@@ -767,6 +772,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           *s_abort = 1;
           break;
         }
+        if (owner && !tried && rows_here > 16)
+          published = __all_sync(0xffffffffu, ld_acquire_gpu(&cnt[1]) == ncontrib - 1);
       }
       tc_fence_after();
 
@@ -877,6 +884,8 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         continue;
       }
       const bool fast = split && named_bar_and(1, kEpiThreads, owner && pre);
+      // An owner whose peers have all published reduces at once (no ticket).
+      const bool fetch = split && !fast && named_bar_and(1, kEpiThreads, owner && published);
       if (!split || fast) {
         // Whole tile, or an owner with its peers' sum ready: final values now.
 #pragma unroll 1
@@ -912,8 +921,12 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         // CTAs that have already arrived (so are running): no co-residency of
         // the grid is assumed.
         if (etid == 0) {
-          const int prev = atom_add_relaxed_gpu(&cnt[0], 1);
-          s_flag[acc.idx] = (prev == ncontrib - 1) ? 1 : 0;
+          if (fetch) {
+            s_flag[acc.idx] = 1;
+          } else {
+            const int prev = atom_add_relaxed_gpu(&cnt[0], 1);
+            s_flag[acc.idx] = (prev == ncontrib - 1) ? 1 : 0;
+          }
         }
         named_bar_sync(1, kEpiThreads);
         const bool reducer = s_flag[acc.idx] != 0;
@@ -949,7 +962,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           if (etid == 0) {
             // Bounded wait for the other ncontrib - 1 partials.
             int ok = 1;
-            if (ld_acquire_gpu(&cnt[1]) != ncontrib - 1) {
+            if (!fetch && ld_acquire_gpu(&cnt[1]) != ncontrib - 1) {
               const uint64_t t0 = globaltimer_ns();
               while (ld_acquire_gpu(&cnt[1]) != ncontrib - 1) {
                 if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
