@@ -1153,9 +1153,13 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const int tp_par = (int)(tp_epoch & 1u);
     const uint32_t tp_tag = tp_epoch + 1u;
     const uint32_t base_sm = smem_u32(lring);
+    // Dense output in one 8-byte store per quad when the rows are 8-byte aligned.
+    const bool vec_out = p.tp_world == 0 && (p.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 7) == 0;
     for (int e = threadIdx.x; e < nq * rows_here; e += Cfg::kThreads) {
       const int c = e / nq;
       const int f = f0 + 4 * (e - c * nq);
+      const int n0 = nt * kBlockN + f;
+      if (n0 >= p.N) continue;  // past the last feature: nothing to load or store
       const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
       float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -1169,9 +1173,22 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         }
       }
       const int m = mt * NTOK + c;
+      if (vec_out && n0 + 3 < p.N) {
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float out = v[j];
+          if (p.bias != nullptr) out += (float)reinterpret_cast<const T*>(p.bias)[n0 + j];
+          const T t = (T)out;
+          h[j] = *reinterpret_cast<const uint16_t*>(&t);
+        }
+        *reinterpret_cast<uint2*>(reinterpret_cast<T*>(p.y) + (int64_t)m * p.ldy + n0) =
+            make_uint2(h[0] | (h[1] << 16), h[2] | (h[3] << 16));
+        continue;
+      }
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const int n = nt * kBlockN + f + j;
+        const int n = n0 + j;
         if (n >= p.N) break;
         if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's (or the owner's) landing slot
           const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
@@ -1186,7 +1203,11 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         }
       }
     }
-    cluster_arrive();
+    // Every value loaded from a peer above has been consumed by a store, so
+    // the loads are complete: a relaxed arrive is enough to tell the peers that
+    // their shared memory is no longer read (no need to wait for the global
+    // stores to be acknowledged).
+    cluster_arrive_relaxed();
     if (p.tp_world > 0) tp_cluster_finish<T>(p, nt * kBlockN + f0, nf, mt * NTOK, rows_here, tp_epoch);
     cluster_wait();
   }

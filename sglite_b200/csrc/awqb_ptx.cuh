@@ -386,6 +386,12 @@ __device__ __forceinline__ void cluster_arrive() {
   __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
+// Arrive without ordering this thread's earlier memory operations (for a
+// barrier that only keeps shared memory alive for completed peer reads).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  __syncwarp();
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() {
   __syncwarp();
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
