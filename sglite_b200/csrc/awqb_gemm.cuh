@@ -134,7 +134,10 @@ struct GemmCfg {
   static constexpr int kBudget = 225 * 1024 - 1024 - 512;
   static constexpr int kSD = kATmem ? cmin(4, (512 - 2 * NTOK) / kAStageCols) : 2;
   static constexpr int kSL = cmin(16, (kBudget - kSD * kWStage) / kLStage);
-  static constexpr int kSmemBytes = 1024 + kSL * kLStage + kSD * kWStage + 512;
+  // Scattered output (MoE): each epilogue warp's copy of the tile's destination
+  // rows and scales, {row or -1, scale bits} per token row.
+  static constexpr int kRowBytes = kNumEpiWarps * NTOK * 8;
+  static constexpr int kSmemBytes = 1024 + kSL * kLStage + kSD * kWStage + 512 + kRowBytes;
   static constexpr int kAcol0 = 2 * NTOK;             // TMEM: [0, 2*NTOK) accumulators, then A stages
   static constexpr int kTmemCols = pow2ceil(cmax(32, 2 * NTOK + (kATmem ? kSD * kAStageCols : 0)));
   static_assert(kSD >= 2, "need two A stages");
@@ -431,6 +434,7 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_flag = reinterpret_cast<volatile int*>(s_tmem + 2);  // [2]
   volatile uint32_t* s_tpe = s_tmem + 4;  // fused all-reduce: this call's counter value
+  int2* row_slots = reinterpret_cast<int2*>(reinterpret_cast<uint8_t*>(bars) + 512);  // [epi warp][NTOK]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -698,20 +702,31 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
         return p.ws_part + ((int64_t)cj * 2 + cs) * (128 * NTOK);
       };
 
-      // Scattered output (MoE): the destination row and scale of the first 16
-      // rows do not depend on the accumulator; fetch them before waiting for it.
-      int pf_m = 0;
-      float pf_s = 1.f;
-      bool pf_ok = false;
+      // Scattered output (MoE): the destination rows and scales of the tile do
+      // not depend on the accumulator. Each warp stages them in its own slots
+      // (two dependent loads per row, all rows in flight) before waiting for it.
+      int2* const rows_sm = row_slots + (warp - Cfg::kEpiWarp0) * NTOK;
       if (p.row_map != nullptr || p.row_scale != nullptr) {
-        const int li = lane & 15;
-        pf_m = mt * NTOK + li;
-        pf_ok = li < rows_here;
-        if (pf_ok && p.row_map != nullptr) {
-          pf_m = p.row_map[pf_m];
-          pf_ok = pf_m < p.num_valid;
+        __syncwarp();  // this warp's reads of the previous tile's slots are done
+        constexpr int kIt = (NTOK + 31) / 32;
+        int rm[kIt];
+#pragma unroll
+        for (int i = 0; i < kIt; ++i) {
+          const int c = lane + 32 * i;
+          int m = mt * NTOK + c;
+          bool ok = c < rows_here;
+          if (ok && p.row_map != nullptr) {
+            m = p.row_map[m];
+            ok = m < p.num_valid;  // padding rows of an expert block
+          }
+          rm[i] = ok ? m : -1;
         }
-        if (pf_ok && p.row_scale != nullptr) pf_s = p.row_scale[pf_m];
+#pragma unroll
+        for (int i = 0; i < kIt; ++i) {
+          const float sc = (rm[i] >= 0 && p.row_scale != nullptr) ? p.row_scale[rm[i]] : 1.f;
+          if (lane + 32 * i < NTOK) rows_sm[lane + 32 * i] = make_int2(rm[i], __float_as_int(sc));
+        }
+        __syncwarp();
       }
 
       // Wait for the accumulator. Meanwhile an owner checks whether its peers
@@ -822,30 +837,14 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
           }
           return;
         }
-        const int li = lane & 15;
-        int my_m = pf_m;
-        float my_s = pf_s;
-        bool my_ok = pf_ok && li < cnt;
-        if (c0 != 0) {
-          my_m = mt * NTOK + c0 + li;
-          my_s = 1.f;
-          my_ok = li < cnt && c0 + li < rows_here;
-          if (my_ok && p.row_map != nullptr) {
-            my_m = p.row_map[my_m];
-            my_ok = my_m < p.num_valid;
-          }
-          if (my_ok && p.row_scale != nullptr) my_s = p.row_scale[my_m];
-        }
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           if (c >= cnt) break;
-          const int m = __shfl_sync(0xffffffffu, my_m, c);
-          const float sc = __shfl_sync(0xffffffffu, my_s, c);
-          const bool ok = __shfl_sync(0xffffffffu, my_ok ? 1 : 0, c) != 0;
-          if (ok && n < p.N) {
+          const int2 rs = rows_sm[c0 + c];  // same address in every lane: broadcast
+          if (rs.x >= 0 && n < p.N) {
             float val = vals[c] + bias_v;
-            if (p.row_scale != nullptr) val *= sc;
-            reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)val;
+            if (p.row_scale != nullptr) val *= __int_as_float(rs.y);
+            reinterpret_cast<T*>(p.y)[(int64_t)rs.x * p.ldy + n] = (T)val;
           }
         }
       };
