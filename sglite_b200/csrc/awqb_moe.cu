@@ -27,53 +27,66 @@ constexpr int kMaxTopk = 32;
 
 // One warp per token. Top-k is chosen on the logits (softmax is monotonic),
 // ties going to the lower expert index, so the choice does not depend on the
-// rounding of exp.
+// rounding of exp. The row lives in registers (expert e = lane + 32 j in slot
+// j, taken experts in a bit mask); lane k keeps the k-th choice. Every sum runs
+// in the same order as a sequential pass (experts ascending per lane, then the
+// shuffle tree; choices in rank order).
 __global__ void topk_softmax_kernel(const float* __restrict__ logits, int M, int E, int topk,
                                     int renormalize, float* __restrict__ w_out,
                                     int32_t* __restrict__ id_out) {
+  constexpr int kSlots = kMaxExperts / 32;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= M) return;
   const float* row = logits + (int64_t)warp * E;
+  float v[kSlots];
+#pragma unroll
+  for (int j = 0; j < kSlots; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? row[e] : -INFINITY;
+  }
   float mx = -INFINITY;
-  for (int e = lane; e < E; e += 32) mx = fmaxf(mx, row[e]);
+#pragma unroll
+  for (int j = 0; j < kSlots; ++j)
+    if (lane + 32 * j < E) mx = fmaxf(mx, v[j]);
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float sum = 0.f;
-  for (int e = lane; e < E; e += 32) sum += expf(row[e] - mx);
+#pragma unroll
+  for (int j = 0; j < kSlots; ++j)
+    if (lane + 32 * j < E) sum += expf(v[j] - mx);
   for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
 
-  uint32_t taken[kMaxExperts / 32] = {};
-  float wsel[kMaxTopk];
-  int isel[kMaxTopk];
+  uint32_t taken = 0;
+  float my_w = 0.f;
+  int my_i = 0;
   float wsum = 0.f;
   for (int k = 0; k < topk; ++k) {
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int e = lane; e < E; e += 32) {
-      if (taken[e >> 5] & (1u << (e & 31))) continue;
-      const float v = row[e];
-      if (v > bv || (v == bv && e < bi)) { bv = v; bi = e; }
+#pragma unroll
+    for (int j = 0; j < kSlots; ++j) {
+      const int e = lane + 32 * j;
+      if (e >= E || (taken & (1u << j))) continue;
+      if (v[j] > bv || (v[j] == bv && e < bi)) { bv = v[j]; bi = e; }
     }
     for (int o = 16; o > 0; o >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
     }
-    taken[bi >> 5] |= 1u << (bi & 31);
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
     const float p = expf(bv - mx) / sum;
-    wsel[k] = p;
-    isel[k] = bi;
+    if (lane == k) { my_w = p; my_i = bi; }
     wsum += p;
   }
-  if (lane == 0) {
-    float* wo = w_out + (int64_t)warp * topk;
-    int32_t* io = id_out + (int64_t)warp * topk;
-    if (renormalize) {
-      float s2 = 0.f;
-      for (int k = 0; k < topk; ++k) { wsel[k] = wsel[k] / wsum; s2 += wsel[k]; }
-      for (int k = 0; k < topk; ++k) wsel[k] = wsel[k] / (s2 + 1e-8f);
-    }
-    for (int k = 0; k < topk; ++k) { wo[k] = wsel[k]; io[k] = isel[k]; }
+  if (renormalize) {
+    float s2 = 0.f;
+    for (int k = 0; k < topk; ++k) s2 += __shfl_sync(0xffffffffu, my_w / wsum, k);
+    my_w = (my_w / wsum) / (s2 + 1e-8f);
+  }
+  if (lane < topk) {
+    w_out[(int64_t)warp * topk + lane] = my_w;
+    id_out[(int64_t)warp * topk + lane] = my_i;
   }
 }
 
