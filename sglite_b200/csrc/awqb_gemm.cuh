@@ -1152,9 +1152,29 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
     const int tp_par = (int)(tp_epoch & 1u);
     const uint32_t tp_tag = tp_epoch + 1u;
     const uint32_t base_sm = smem_u32(lring);
+    // Fused all-reduce: one feature per thread, so that the thread that sends a
+    // value is the one that later waits for that value's words (its own rank's
+    // word is then its own store: no extra round trip to see it).
+    for (int e = threadIdx.x; p.tp_world > 0 && e < nf * rows_here; e += Cfg::kThreads) {
+      const int c = e / nf;
+      const int f = f0 + (e - c * nf);
+      const int n = nt * kBlockN + f;
+      if (n >= p.N) continue;
+      const uint32_t off = base_sm + (uint32_t)((c * 128 + f) * 4);
+      float v = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < S) v += ld_dsmem_f32(mapa_shared(off, (uint32_t)r));
+      const int m = mt * NTOK + c;
+      const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
+      if (p.tp_rsag)
+        st_tagged_sys(p.tp_land[nt % p.tp_world] + o, v, tp_tag);
+      else
+        for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tp_tag);
+    }
     // Dense output in one 8-byte store per quad when the rows are 8-byte aligned.
-    const bool vec_out = p.tp_world == 0 && (p.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 7) == 0;
-    for (int e = threadIdx.x; e < nq * rows_here; e += Cfg::kThreads) {
+    const bool vec_out = (p.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 7) == 0;
+    for (int e = threadIdx.x; p.tp_world == 0 && e < nq * rows_here; e += Cfg::kThreads) {
       const int c = e / nq;
       const int f = f0 + 4 * (e - c * nq);
       const int n0 = nt * kBlockN + f;
@@ -1189,17 +1209,9 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
       for (int j = 0; j < 4; ++j) {
         const int n = n0 + j;
         if (n >= p.N) break;
-        if (p.tp_world > 0) {  // fused all-reduce: this value to every rank's (or the owner's) landing slot
-          const int64_t o = (int64_t)tp_par * p.tp_half + ((int64_t)p.tp_rank * p.tp_rows + m) * p.N + n;
-          if (p.tp_rsag)
-            st_tagged_sys(p.tp_land[nt % p.tp_world] + o, v[j], tp_tag);
-          else
-            for (int d = 0; d < p.tp_world; ++d) st_tagged_sys(p.tp_land[d] + o, v[j], tp_tag);
-        } else {
-          float out = v[j];
-          if (p.bias != nullptr) out += (float)reinterpret_cast<const T*>(p.bias)[n];
-          reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)out;
-        }
+        float out = v[j];
+        if (p.bias != nullptr) out += (float)reinterpret_cast<const T*>(p.bias)[n];
+        reinterpret_cast<T*>(p.y)[(int64_t)m * p.ldy + n] = (T)out;
       }
     }
     // Every value loaded from a peer above has been consumed by a store, so
