@@ -656,6 +656,31 @@ def run_moe(args):
                       "per_m": per, "peak_hbm_GBps": hbm, "peak_tflops": tflops_peak, "peak_kind": kind}), flush=True)
 
 
+def run_norm(args):
+    """Residual-add RMSNorm after the row-parallel projections (the reference's
+    RMSNormFused, layers/norm.py:28-47), hidden 8192 (config 3), bf16. HBM-bound:
+    algorithmic bytes = 4 * M * N * 2 (read x and residual, write both) + N * 2."""
+    from sglite_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    N = 8192
+    hbm, _, kind = _peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    per = {}
+    for M in (1, 32, 256, 4096, 32768):
+        x = torch.randn((M, N), generator=g, device=dev).to(DTYPE)
+        r = torch.randn((M, N), generator=g, device=dev).to(DTYPE)
+        w = (torch.rand(N, generator=g, device=dev) + 0.5).to(DTYPE)
+        us = _graph_us(lambda: ops.fused_add_rmsnorm(x, r, w, 1e-6), args.warmup, args.steps, reps=16)
+        nbytes = 4 * M * N * 2 + N * 2
+        per[f"M{M}"] = {"us": round(us, 3), "GBps": round(nbytes / us / 1e3, 1),
+                        "frac_hbm": round(nbytes / us / 1e3 / hbm, 3)}
+    print(json.dumps({"workload": "fused_add_rmsnorm hidden 8192 (after the row-parallel all-reduce)",
+                      "metric": "us per call", "unit": "us", "per_m": per, "peak_hbm_GBps": hbm,
+                      "peak_kind": kind, "l2": "M <= 4096 fits in L2 between calls; M = 32768 (1 GB) does not"}),
+          flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -663,7 +688,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe", "gemm"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "single", "tp70b", "moe", "gemm", "norm"],
                     help="decode (default, the contract line) or another BASELINE config")
     ap.add_argument("--allreduce", default="fused", choices=["fused", "nccl"],
                     help="row-parallel all-reduce at N > 1: fused into the GEMM over peer memory, or NCCL")
@@ -684,6 +709,8 @@ def main():
         run_tp70b(args)
     elif args.workload == "moe":
         run_moe(args)
+    elif args.workload == "norm":
+        run_norm(args)
     elif args.workload == "gemm":
         run_gemm(args)
     else:

@@ -177,6 +177,24 @@ int awqb_moe_topk_sum(const void* in, int64_t M, int64_t topk, int64_t H, const 
                       int64_t e_begin, int64_t e_end, int dtype, void* out, void* stream);
 
 /* ------------------------------------------------------------------------
+ * RMSNorm after a projection. Replace flashinfer.rmsnorm and
+ * flashinfer.fused_add_rmsnorm as called by RMSNorm / RMSNormFused,
+ * srt/model_executor/layers/norm.py:10-47 (arithmetic of flashinfer 0.6.11,
+ * include/flashinfer/norm.cuh): per row, x = input (+ residual) in fp32,
+ * out = x * rsqrt(mean(x * x) + eps) * weight, rounded to the dtype.
+ * N (features) is a multiple of 8 and at most 16384; row strides ld_* are in
+ * elements, multiples of 8; all pointers 16-byte aligned. The kernels are
+ * launched with programmatic dependent launch after a GEMM on the same stream.
+ * ------------------------------------------------------------------------ */
+/* out[m] = RMSNorm(input[m]) * weight (out may equal input). */
+int awqb_rmsnorm(const void* input, const void* weight, void* out, int64_t M, int64_t N, int64_t ld_in,
+                 int64_t ld_out, float eps, int dtype, void* stream);
+/* In place: residual[m] = input[m] + residual[m] (rounded), then
+ * input[m] = RMSNorm(fp32 sum) * weight. */
+int awqb_fused_add_rmsnorm(void* input, void* residual, const void* weight, int64_t M, int64_t N,
+                           int64_t ld_in, int64_t ld_res, float eps, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel all-reduce. Replaces NCCLWrapper (create_nccl_uid, ctor,
  * all_reduce), kernels/csrc/src/pynccl.cu:75-189, used through
  * PyNCCLDistributedImpl.all_reduce, srt/distributed/communicator.py:62-65.

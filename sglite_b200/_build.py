@@ -27,6 +27,7 @@ SOURCES = [
     "awqb_repack.cu",
     "awqb_gemm.cu",
     "awqb_moe.cu",
+    "awqb_norm.cu",
     "awqb_nccl.cpp",
 ]
 

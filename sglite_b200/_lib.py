@@ -56,6 +56,9 @@ _SIGNATURES = {
     ),
     "awqb_silu_and_mul": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp]),
     "awqb_silu_and_mul_interleaved": (c_int, [c_vp, c_i64, c_vp, c_i64, c_int, c_vp, c_vp]),
+    "awqb_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, ctypes.c_float, c_int, c_vp]),
+    "awqb_fused_add_rmsnorm": (c_int, [c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, ctypes.c_float, c_int,
+                                       c_vp]),
     "awqb_moe_topk_sum": (c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_i64, c_int, c_vp, c_vp]),
     "awqb_nccl_unique_id_bytes": (c_int, []),
     "awqb_nccl_get_unique_id": (c_int, [c_vp]),

@@ -420,6 +420,63 @@ def silu_and_mul(h: torch.Tensor, rows_dev: Optional[torch.Tensor] = None,
     return out
 
 
+def _check_device(*ts: torch.Tensor) -> torch.device:
+    """Same CUDA device for all (layout is checked by the caller)."""
+    dev = ts[0].device
+    for t in ts:
+        if t.device.type != "cuda":
+            raise ValueError("tensors must live on a CUDA device (there is no CPU path)")
+        if t.device != dev:
+            raise ValueError("tensors must live on the same device")
+    return dev
+
+
+def _rows_2d(t: torch.Tensor, N: int) -> Tuple[torch.Tensor, int]:
+    """[..., N] -> ([M, N] view of the same memory, row stride in elements)."""
+    if t.shape[-1] != N or t.stride(-1) != 1:
+        raise ValueError("the last dimension must be the contiguous feature dimension")
+    if t.dim() == 2:
+        t2 = t
+    elif t.is_contiguous():
+        t2 = t.view(-1, N)
+    else:
+        raise ValueError("tensors with more than 2 dimensions must be contiguous")
+    return t2, (t2.stride(0) if t2.shape[0] > 1 else N)
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """x * rsqrt(mean(x^2) + eps) * weight over the last dimension, fp32 inside
+    (flashinfer.rmsnorm semantics)."""
+    N = x.shape[-1]
+    if weight.numel() != N or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [N] tensor in the activation dtype")
+    dev = _check_device(x, weight)
+    x2, ldx = _rows_2d(x, N)
+    if out is None:
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    o2, ldo = _rows_2d(out, N)
+    with _DeviceGuard(dev):
+        call("awqb_rmsnorm", _p(x2), _p(weight), _p(o2), x2.shape[0], N, ldx, ldo, float(eps),
+             _dtype_code(x.dtype), _stream(dev))
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float) -> None:
+    """In place: residual += x; x = rmsnorm(residual) * weight, the norm taken
+    over the fp32 sum (flashinfer.fused_add_rmsnorm semantics)."""
+    N = x.shape[-1]
+    if residual.shape != x.shape or residual.dtype != x.dtype:
+        raise ValueError("residual must have the shape and dtype of x")
+    if weight.numel() != N or weight.dtype != x.dtype or not weight.is_contiguous():
+        raise ValueError("weight must be a contiguous [N] tensor in the activation dtype")
+    dev = _check_device(x, residual, weight)
+    x2, ldx = _rows_2d(x, N)
+    r2, ldr = _rows_2d(residual, N)
+    with _DeviceGuard(dev):
+        call("awqb_fused_add_rmsnorm", _p(x2), _p(r2), _p(weight), x2.shape[0], N, ldx, ldr, float(eps),
+             _dtype_code(x.dtype), _stream(dev))
+
+
 def moe_topk_sum(y3: torch.Tensor, M: int, topk: int, topk_ids: Optional[torch.Tensor], e_begin: int,
                  e_end: int, out: torch.Tensor) -> torch.Tensor:
     dev = _check_cuda(y3, out)

@@ -68,6 +68,31 @@ def test_gemm_rejects_bad_arguments_without_touching_the_gpu():
     assert b"workspace too small" in lib.awqb_last_error()
 
 
+def test_norm_rejects_bad_arguments_without_touching_the_gpu():
+    lib = _lib.lib()
+    # N not a multiple of 8, N over the register-resident maximum
+    assert lib.awqb_rmsnorm(None, None, None, 1, 12, 12, 12, 1e-6, 1, None) == 1
+    assert lib.awqb_rmsnorm(None, None, None, 1, 16392, 16392, 16392, 1e-6, 1, None) == 1
+    # row stride below N
+    assert lib.awqb_fused_add_rmsnorm(None, None, None, 1, 4096, 2048, 4096, 1e-6, 1, None) == 1
+    # null pointers, misaligned input
+    assert lib.awqb_fused_add_rmsnorm(None, None, None, 1, 4096, 4096, 4096, 1e-6, 1, None) == 1
+    assert lib.awqb_rmsnorm(ctypes.c_void_p(8), ctypes.c_void_p(256), ctypes.c_void_p(256), 1, 4096, 4096, 4096,
+                            1e-6, 1, None) == 1
+    assert b"16-byte" in lib.awqb_last_error()
+    # no rows: nothing to do
+    assert lib.awqb_rmsnorm(None, None, None, 0, 4096, 4096, 4096, 1e-6, 1, None) == 0
+
+
+def test_norm_layers_mirror_reference_interface():
+    from sglite_b200.norm import RMSNorm, RMSNormFused
+
+    for cls in (RMSNorm, RMSNormFused):
+        layer = cls(4096, 1e-6)
+        assert layer.weight.shape == (4096,) and layer.eps == 1e-6
+    assert hasattr(RMSNorm, "forward_inplace")
+
+
 def test_config_matches_reference_semantics():
     cfg = AWQB200Config.from_config({"w_bit": 4, "q_group_size": 128, "zero_point": True})
     assert cfg.get_name() == "awq_b200" and cfg.pack_factor == 8

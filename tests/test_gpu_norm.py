@@ -1,0 +1,127 @@
+"""RMSNorm and residual-add RMSNorm on the GPU against the CPU restatement of
+flashinfer's arithmetic (the reference's layers/norm.py:10-47 calls it). The
+rounded residual must match exactly; the normalised output within
+max|y - ref| <= 1e-2 * max|ref| (the sum of squares is reduced in a different
+order, and rsqrt is the hardware approximation)."""
+
+import pytest
+import torch
+
+from oracle.awq_ref import awq_linear_ref, rel_err
+from oracle.norm_ref import rmsnorm_ref
+from sglite_b200 import ops
+from sglite_b200.norm import RMSNorm, RMSNormFused
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def _data(M, N, dtype, seed, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn((M, N), generator=g) * scale).to(dtype)
+    r = (torch.randn((M, N), generator=g) * 2.0).to(dtype)
+    w = (torch.rand(N, generator=g) + 0.5).to(dtype)
+    return x, r, w
+
+
+@pytest.mark.parametrize("N", [8, 1024, 2056, 4096, 8192, 16384])
+@pytest.mark.parametrize("M", [1, 7, 64, 300])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_add_rmsnorm(cuda, M, N, dtype):
+    x, r, w = _data(M, N, dtype, seed=M * 7 + N)
+    ref_out, ref_res = rmsnorm_ref(x, w, 1e-6, residual=r)
+    xd, rd, wd = x.to(cuda), r.to(cuda), w.to(cuda)
+    ops.fused_add_rmsnorm(xd, rd, wd, 1e-6)
+    assert torch.equal(rd.cpu(), ref_res)          # residual: exact
+    assert rel_err(xd, ref_out) <= TOL             # normalised output, in place
+
+
+@pytest.mark.parametrize("N", [8, 4096, 16384])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_rmsnorm_out_of_place_and_in_place(cuda, N, dtype):
+    x, _, w = _data(33, N, dtype, seed=N, scale=3.0)
+    ref, _ = rmsnorm_ref(x, w, 1e-5)
+    xd, wd = x.to(cuda), w.to(cuda)
+    y = ops.rmsnorm(xd, wd, 1e-5)
+    assert rel_err(y, ref) <= TOL and torch.equal(xd.cpu(), x)
+    ops.rmsnorm(xd, wd, 1e-5, out=xd)
+    assert torch.equal(xd.cpu(), y.cpu())
+
+
+def test_strided_rows_and_batch_dims(cuda):
+    N, dtype = 2048, torch.bfloat16
+    x, r, w = _data(12, N, dtype, seed=5)
+    ref_out, ref_res = rmsnorm_ref(x, w, 1e-6, residual=r)
+    big = torch.zeros((12, N + 64), dtype=dtype, device=cuda)   # rows N + 64 apart
+    big[:, :N] = x.to(cuda)
+    xv = big[:, :N]
+    rd = r.to(cuda).view(3, 4, N)
+    ops.fused_add_rmsnorm(xv, rd.view(12, N), w.to(cuda), 1e-6)
+    assert torch.equal(rd.view(12, N).cpu(), ref_res)
+    assert rel_err(xv, ref_out) <= TOL
+    assert torch.count_nonzero(big[:, N:]) == 0                  # the padding columns are untouched
+    y3 = ops.rmsnorm(x.to(cuda).view(3, 4, N), w.to(cuda), 1e-6)
+    assert y3.shape == (3, 4, N)
+    assert rel_err(y3.view(12, N), rmsnorm_ref(x, w, 1e-6)[0]) <= TOL
+
+
+def test_layers_follow_reference_semantics(cuda):
+    N, dtype = 4096, torch.bfloat16
+    x, r, w = _data(5, N, dtype, seed=11)
+    layer = RMSNormFused(N, 1e-6)
+    layer.weight = w.to(cuda)
+    xd, rd = x.to(cuda), r.to(cuda)
+    out, res = layer.forward(xd)              # no residual: (rmsnorm(x), x)
+    assert res is xd and rel_err(out, rmsnorm_ref(x, w, 1e-6)[0]) <= TOL
+    out, res = layer.forward(xd, rd)          # residual: both in place
+    ref_out, ref_res = rmsnorm_ref(x, w, 1e-6, residual=r)
+    assert out is xd and res is rd and torch.equal(rd.cpu(), ref_res) and rel_err(xd, ref_out) <= TOL
+    plain = RMSNorm(N, 1e-6)
+    plain.weight = w.to(cuda)
+    y = x.to(cuda)
+    plain.forward_inplace(y)
+    assert rel_err(y, rmsnorm_ref(x, w, 1e-6)[0]) <= TOL
+
+
+def test_after_fused_gemm_allreduce_in_a_graph(cuda):
+    """The row-parallel chain of a decoder layer: GEMM + all-reduce in one kernel
+    (exchange of world size 1), then residual add + RMSNorm, captured in a CUDA
+    graph and replayed; checked against the oracles of both steps."""
+    from sglite_b200.distributed import init_peer_exchange
+    from sglite_b200.synthetic import make_activations, make_awq_weights
+
+    K, N, G, M, dtype = 2048, 4096, 128, 8, torch.bfloat16
+    wq = make_awq_weights(K, N, G, dtype, seed=3)
+    blob = ops.repack(*(wq[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
+    x = make_activations(M, K, dtype, seed=4)
+    _, r, w = _data(M, N, dtype, seed=6)
+    ex = init_peer_exchange(tp_rank=0, tp_size=1, tp_cpu_group=None, device=cuda, max_rows=64, max_n=N)
+    try:
+        xd, wd = x.to(cuda), w.to(cuda)
+        y = torch.empty((M, N), dtype=dtype, device=cuda)
+        res = torch.empty((M, N), dtype=dtype, device=cuda)
+
+        def layer():
+            ex.gemm_allreduce(xd, blob, K, N, G, out=y)
+            ops.fused_add_rmsnorm(y, res, wd, 1e-6)
+
+        res.copy_(r.to(cuda))
+        layer()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer()
+        gemm_ref = awq_linear_ref(x, wq["qweight"], wq["qzeros"], wq["scales"], G)
+        for _ in range(3):
+            res.copy_(r.to(cuda))
+            g.replay()
+            torch.cuda.synchronize()
+            ref_out, ref_res = rmsnorm_ref(y_gemm := ops.gemm(xd, blob, K, N, G), w, 1e-6, residual=r)
+            assert rel_err(y_gemm, gemm_ref) <= TOL
+            assert torch.equal(res.cpu(), ref_res)
+            assert rel_err(y, ref_out) <= TOL
+        del g
+        assert ops.device_error() == 0
+    finally:
+        ex.destroy()
