@@ -200,16 +200,22 @@ __device__ __forceinline__ float to_f(T v) { return (float)v; }
 
 // out[r, j] = silu(in[r, j]) * in[r, I + j], computed in fp32; eight
 // elements (16 bytes) per thread and iteration (I % 8 == 0).
+// silu(g) = g / (1 + e^-g) with the hardware exp2 and divide approximations
+// (relative error ~1e-6, far below the fp16/bf16 rounding of the result): the
+// exact expf and division would make this copy-like kernel issue-bound.
 template <typename T, bool kInterleaved>
 __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
                                     const int32_t* __restrict__ rows_dev, int I, T* __restrict__ out) {
   int64_t rows = rows_max;
   if (rows_dev != nullptr && (int64_t)*rows_dev < rows) rows = *rows_dev;
   const int iv = I / 8;
-  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < rows * iv;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = t / iv;
-    const int j = (int)(t - r * iv) * 8;
+  // 32-bit index arithmetic (a 64-bit division per 16-byte vector would cost
+  // more than the memory traffic); the host checks rows_max * I / 8 < 2^31.
+  const uint32_t total = (uint32_t)(rows * iv);
+  for (uint32_t t = blockIdx.x * blockDim.x + threadIdx.x; t < total; t += gridDim.x * blockDim.x) {
+    const uint32_t r32 = t / (uint32_t)iv;
+    const int64_t r = r32;
+    const int j = (int)(t - r32 * (uint32_t)iv) * 8;
     uint4 ov;
     T* o = reinterpret_cast<T*>(&ov);
     if constexpr (kInterleaved) {  // columns 2j = gate j, 2j + 1 = up j
@@ -221,7 +227,7 @@ __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
       for (int i = 0; i < 8; ++i) {
         const T* pr = i < 4 ? pa + 2 * i : pb + 2 * (i - 4);
         const float gf = to_f(pr[0]);
-        o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(pr[1]));
+        o[i] = (T)(__fdividef(gf, 1.0f + __expf(-gf)) * to_f(pr[1]));
       }
     } else {
       const uint4 gv = *reinterpret_cast<const uint4*>(in + r * 2 * I + j);
@@ -231,7 +237,7 @@ __global__ void silu_and_mul_kernel(const T* __restrict__ in, int64_t rows_max,
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float gf = to_f(g[i]);
-        o[i] = (T)(gf / (1.0f + expf(-gf)) * to_f(u[i]));
+        o[i] = (T)(__fdividef(gf, 1.0f + __expf(-gf)) * to_f(u[i]));
       }
     }
     *reinterpret_cast<uint4*>(out + r * I + j) = ov;
@@ -349,6 +355,7 @@ int silu_and_mul_impl(const void* in, int64_t rows_max, const int32_t* rows_dev,
                "in and out must be 16-byte aligned");
   AWQB_REQUIRE(in && out, kInvalidArgument, "null pointer");
   if (rows_max == 0) return kOk;
+  AWQB_REQUIRE(rows_max * (I / 8) < (1ll << 31), kInvalidArgument, "too many elements (rows * I / 8 >= 2^31)");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned g = grid1d(rows_max * (I / 8), 256);
   if (dtype == AWQB_DTYPE_F16) {
