@@ -124,6 +124,15 @@ int64_t awqb_moe_max_padded(int64_t numel, int64_t num_experts, int64_t block_m)
 int awqb_moe_align(const int32_t* topk_ids, int64_t numel, int64_t e_begin, int64_t e_end,
                    int64_t block_m, int32_t* sorted_ids, int64_t max_padded,
                    int32_t* block_expert, int32_t* num_post_pad, void* stream);
+/* The same result computed by many CTAs (chunk histograms, one scan CTA, one
+ * warp per chunk for the stable scatter): for large inputs (thousands of pairs),
+ * where one CTA is bound by a single SM. Needs a caller-owned workspace of
+ * awqb_moe_align_workspace_bytes(numel, e_end - e_begin) bytes (per-chunk
+ * counts; no zeroing needed). Replaces moe_align_block_size, fused.py:34-61. */
+int64_t awqb_moe_align_workspace_bytes(int64_t numel, int64_t num_experts);
+int awqb_moe_align_ex(const int32_t* topk_ids, int64_t numel, int64_t e_begin, int64_t e_end,
+                      int64_t block_m, int32_t* sorted_ids, int64_t max_padded, int32_t* block_expert,
+                      int32_t* num_post_pad, void* workspace, int64_t workspace_bytes, void* stream);
 /* out[r] = x[sorted_ids[r] / topk] (zero for padding rows), r < *num_post_pad.
  * Stands in for the row gather done by fused_moe_kernel's a_ptrs,
  * kernels/triton/fused_moe.py:241. */

@@ -43,6 +43,8 @@ _SIGNATURES = {
     "awqb_moe_topk_softmax": (c_int, [c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp]),
     "awqb_moe_max_padded": (c_i64, [c_i64, c_i64, c_i64]),
     "awqb_moe_align": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp]),
+    "awqb_moe_align_workspace_bytes": (c_i64, [c_i64, c_i64]),
+    "awqb_moe_align_ex": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "awqb_moe_gather_rows": (c_int, [c_vp, c_i64, c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_vp]),
     "awqb_moe_grouped_workspace_bytes": (c_int, [c_i64, c_i64, c_i64, c_i64, c_int, c_i64p]),
     "awqb_gemm_silu_mul": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_vp]),

@@ -179,6 +179,118 @@ __global__ void __launch_bounds__(1024) align_kernel(const int32_t* __restrict__
   }
 }
 
+// Multi-CTA variant for large inputs (same output, same stable order): one
+// CTA counts each chunk of kAlignChunk ids, one CTA turns the counts into
+// padded expert offsets and per-chunk write bases, and one warp per chunk
+// writes its ids in index order. A single CTA would be bound by one SM's
+// shared-memory atomics and match instructions.
+constexpr int kAlignChunk = 1024;
+
+__global__ void __launch_bounds__(256) align_hist_kernel(const int32_t* __restrict__ ids, int numel, int e_begin,
+                                                         int E, int32_t* __restrict__ hist) {
+  extern __shared__ int32_t h[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  const int i0 = blockIdx.x * kAlignChunk;
+  int ev[kAlignChunk / 256];
+#pragma unroll
+  for (int j = 0; j < kAlignChunk / 256; ++j) {
+    const int i = i0 + j * 256 + threadIdx.x;
+    ev[j] = i < numel ? ids[i] - e_begin : -1;
+  }
+#pragma unroll
+  for (int j = 0; j < kAlignChunk / 256; ++j)
+    if (ev[j] >= 0 && ev[j] < E) atomicAdd(&h[ev[j]], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(int64_t)blockIdx.x * E + e] = h[e];
+}
+
+// One CTA, one thread per expert (blockDim = E rounded up to a warp).
+__global__ void align_scan_kernel(int32_t* __restrict__ hist, int nch, int E, int block_m, int numel,
+                                  int max_padded, int32_t* __restrict__ sorted_ids,
+                                  int32_t* __restrict__ block_expert, int32_t* __restrict__ num_post_pad) {
+  __shared__ int32_t off[kMaxExperts + 1];
+  __shared__ int32_t wsum[32];
+  const int e = threadIdx.x, warp = e >> 5, lane = e & 31;
+  // counts of 8 chunks in flight at a time (independent loads)
+  int tot = 0;
+  if (e < E) {
+    for (int c0 = 0; c0 < nch; c0 += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = c0 + j < nch ? hist[(int64_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) tot += v[j];
+    }
+  }
+  const int padded = e < E ? (tot + block_m - 1) / block_m * block_m : 0;
+  int incl = padded;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (e == 0) {
+    int run = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+      const int t = wsum[w];
+      wsum[w] = run;
+      run += t;
+    }
+    off[E] = run;
+    *num_post_pad = run;
+  }
+  __syncthreads();
+  if (e < E) off[e] = wsum[warp] + incl - padded;
+  __syncthreads();
+  if (e < E) {
+    int run = off[e];
+    for (int c0 = 0; c0 < nch; c0 += 8) {  // per-chunk write bases, in chunk order
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = c0 + j < nch ? hist[(int64_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (c0 + j < nch) hist[(int64_t)(c0 + j) * E + e] = run;
+        run += v[j];
+      }
+    }
+    for (int q = off[e] + tot; q < off[e + 1]; ++q) sorted_ids[q] = numel;  // padding of this expert
+    for (int b = off[e] / block_m; b < off[e + 1] / block_m; ++b) block_expert[b] = e;
+  }
+  for (int q = off[E] + e; q < max_padded; q += blockDim.x) sorted_ids[q] = numel;  // unused tail
+}
+
+// One warp per chunk: its ids (loaded at once) in groups of 32, in index order.
+__global__ void __launch_bounds__(32) align_scatter_kernel(const int32_t* __restrict__ ids, int numel, int e_begin,
+                                                           int E, const int32_t* __restrict__ bases,
+                                                           int32_t* __restrict__ sorted_ids) {
+  extern __shared__ int32_t wpos[];
+  const int lane = threadIdx.x;
+  for (int e = lane; e < E; e += 32) wpos[e] = bases[(int64_t)blockIdx.x * E + e];
+  const int i0 = blockIdx.x * kAlignChunk;
+  int ev[kAlignChunk / 32];
+#pragma unroll
+  for (int j = 0; j < kAlignChunk / 32; ++j) {
+    const int i = i0 + 32 * j + lane;
+    const int e = i < numel ? ids[i] - e_begin : -1;
+    ev[j] = (e >= 0 && e < E) ? e : -1;
+  }
+  __syncwarp();
+  const unsigned lt = (1u << lane) - 1u;
+#pragma unroll
+  for (int j = 0; j < kAlignChunk / 32; ++j) {
+    const int e = ev[j];
+    const unsigned grp = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) sorted_ids[wpos[e] + __popc(grp & lt)] = i0 + 32 * j + lane;
+    __syncwarp();
+    if (e >= 0 && (grp & lt) == 0) wpos[e] += __popc(grp);
+    __syncwarp();
+  }
+}
+
 // x_sorted[r] = x[sorted_ids[r] / topk] for live rows, zero for padding rows.
 __global__ void gather_rows_kernel(const uint4* __restrict__ x, const int32_t* __restrict__ sorted_ids,
                                    const int32_t* __restrict__ num_post_pad, int numel, int topk,
@@ -327,6 +439,45 @@ extern "C" int awqb_moe_align(const int32_t* topk_ids, int64_t numel, int64_t e_
       topk_ids, (int)numel, (int)e_begin, (int)e_end, (int)block_m, (int)max_padded, sorted_ids,
       block_expert, num_post_pad);
   AWQB_LAUNCH_CHECK();
+  return kOk;
+}
+
+extern "C" int64_t awqb_moe_align_workspace_bytes(int64_t numel, int64_t num_experts) {
+  const int64_t nch = (numel + kAlignChunk - 1) / kAlignChunk;
+  return nch * num_experts * (int64_t)sizeof(int32_t);
+}
+
+extern "C" int awqb_moe_align_ex(const int32_t* topk_ids, int64_t numel, int64_t e_begin, int64_t e_end,
+                                 int64_t block_m, int32_t* sorted_ids, int64_t max_padded, int32_t* block_expert,
+                                 int32_t* num_post_pad, void* workspace, int64_t workspace_bytes, void* stream) {
+  const int64_t E = e_end - e_begin;
+  AWQB_REQUIRE(E >= 1 && E <= kMaxExperts && e_begin >= 0, kInvalidArgument,
+               "bad expert range [%lld, %lld)", (long long)e_begin, (long long)e_end);
+  AWQB_REQUIRE(block_m >= 1 && numel >= 0 && numel < (1ll << 30), kInvalidArgument, "bad sizes");
+  AWQB_REQUIRE(max_padded >= numel + E * (block_m - 1), kInvalidArgument,
+               "sorted_ids too small: %lld < %lld", (long long)max_padded,
+               (long long)(numel + E * (block_m - 1)));
+  AWQB_REQUIRE(sorted_ids && block_expert && num_post_pad && (numel == 0 || topk_ids), kInvalidArgument,
+               "null pointer");
+  const int64_t need = awqb_moe_align_workspace_bytes(numel, E);
+  AWQB_REQUIRE(workspace != nullptr && workspace_bytes >= need, kInvalidArgument,
+               "workspace too small: %lld < %lld bytes", (long long)workspace_bytes, (long long)need);
+  const int nch = (int)((numel + kAlignChunk - 1) / kAlignChunk);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int32_t* hist = static_cast<int32_t*>(workspace);
+  if (nch > 0) {
+    align_hist_kernel<<<nch, 256, E * sizeof(int32_t), st>>>(topk_ids, (int)numel, (int)e_begin, (int)E, hist);
+    AWQB_LAUNCH_CHECK();
+  }
+  const int threads = (int)((E + 31) / 32 * 32);
+  align_scan_kernel<<<1, threads, 0, st>>>(hist, nch, (int)E, (int)block_m, (int)numel, (int)max_padded,
+                                           sorted_ids, block_expert, num_post_pad);
+  AWQB_LAUNCH_CHECK();
+  if (nch > 0) {
+    align_scatter_kernel<<<nch, 32, E * sizeof(int32_t), st>>>(topk_ids, (int)numel, (int)e_begin, (int)E, hist,
+                                                               sorted_ids);
+    AWQB_LAUNCH_CHECK();
+  }
   return kOk;
 }
 

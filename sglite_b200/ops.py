@@ -275,9 +275,14 @@ def moe_max_padded(numel: int, num_experts: int, block_m: int) -> int:
     return int(lib().awqb_moe_max_padded(numel, num_experts, block_m))
 
 
-def moe_align(topk_ids: torch.Tensor, e_begin: int, e_end: int, block_m: int):
+ALIGN_MULTI_CTA_MIN = 8192  # pairs from which the multi-CTA sort is faster (measured on B200)
+
+
+def moe_align(topk_ids: torch.Tensor, e_begin: int, e_end: int, block_m: int,
+              multi_cta: Optional[bool] = None):
     """Expert-sorted (token, k) ids padded per expert to block_m; returns
-    (sorted_ids [max_padded], block_expert [max_padded / block_m], num_post_pad [1])."""
+    (sorted_ids [max_padded], block_expert [max_padded / block_m], num_post_pad [1]).
+    multi_cta: None picks by size; True / False force one of the two (identical) sorts."""
     ids = topk_ids.contiguous()
     dev = _check_cuda(ids)
     numel = ids.numel()
@@ -285,9 +290,17 @@ def moe_align(topk_ids: torch.Tensor, e_begin: int, e_end: int, block_m: int):
     sorted_ids = torch.empty(maxp, dtype=torch.int32, device=dev)
     block_expert = torch.empty((maxp + block_m - 1) // block_m, dtype=torch.int32, device=dev)
     npp = torch.empty(1, dtype=torch.int32, device=dev)
+    if multi_cta is None:
+        multi_cta = numel >= ALIGN_MULTI_CTA_MIN
     with _DeviceGuard(dev):
-        call("awqb_moe_align", _p(ids), numel, e_begin, e_end, block_m, _p(sorted_ids), maxp,
-             _p(block_expert), _p(npp), _stream(dev))
+        if multi_cta:
+            wsb = int(lib().awqb_moe_align_workspace_bytes(numel, e_end - e_begin))
+            ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=dev)
+            call("awqb_moe_align_ex", _p(ids), numel, e_begin, e_end, block_m, _p(sorted_ids), maxp,
+                 _p(block_expert), _p(npp), _p(ws), ws.numel(), _stream(dev))
+        else:
+            call("awqb_moe_align", _p(ids), numel, e_begin, e_end, block_m, _p(sorted_ids), maxp,
+                 _p(block_expert), _p(npp), _stream(dev))
     return sorted_ids, block_expert, npp
 
 

@@ -25,12 +25,16 @@ def test_topk_softmax_matches_oracle(cuda, M, E, k, renorm):
     assert torch.allclose(w.cpu(), w_ref, rtol=1e-5, atol=1e-7)
 
 
-@pytest.mark.parametrize("M,E,k,bm", [(1, 128, 8, 16), (16, 128, 8, 16), (256, 128, 8, 32), (999, 16, 4, 64)])
+@pytest.mark.parametrize("M,E,k,bm", [(1, 128, 8, 16), (16, 128, 8, 16), (256, 128, 8, 32), (999, 16, 4, 64),
+                                      (4096, 128, 8, 128), (2050, 64, 8, 64)])
 @pytest.mark.parametrize("ep", [None, (4, 12)])
-def test_align_matches_oracle_exactly(cuda, M, E, k, bm, ep):
+@pytest.mark.parametrize("multi", [False, True])
+def test_align_matches_oracle_exactly(cuda, M, E, k, bm, ep, multi):
+    """Both sorts (one CTA; chunk histograms + scan + per-chunk scatter) give the
+    oracle's stable order, padding and block experts."""
     ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(i))[:k] for i in range(M)]).to(torch.int32)
     e0, e1 = ep if ep is not None else (0, E)
-    sorted_ids, block_expert, npp = ops.moe_align(ids.to(cuda), e0, e1, bm)
+    sorted_ids, block_expert, npp = ops.moe_align(ids.to(cuda), e0, e1, bm, multi_cta=multi)
     s_ref, b_ref, n_ref = moe_align_ref(ids, bm, e0, e1)
     n = int(npp.item())
     assert n == n_ref
