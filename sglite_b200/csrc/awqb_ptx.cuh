@@ -381,11 +381,7 @@ __device__ __forceinline__ void cluster_sync_all() {
   __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-// The two halves of cluster_sync_all, for work in between.
-__device__ __forceinline__ void cluster_arrive() {
-  __syncwarp();
-  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
+// Halves of cluster_sync_all, for work in between.
 // Arrive without ordering this thread's earlier memory operations (for a
 // barrier that only keeps shared memory alive for completed peer reads).
 __device__ __forceinline__ void cluster_arrive_relaxed() {
