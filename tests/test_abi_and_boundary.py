@@ -84,6 +84,17 @@ def test_norm_rejects_bad_arguments_without_touching_the_gpu():
     assert lib.awqb_rmsnorm(None, None, None, 0, 4096, 4096, 4096, 1e-6, 1, None) == 0
 
 
+def test_moe_align_ex_checks_its_workspace_without_touching_the_gpu():
+    lib = _lib.lib()
+    need = lib.awqb_moe_align_workspace_bytes(32768, 128)
+    assert need == 32 * 128 * 4  # one count per (1024-pair chunk, expert)
+    p = ctypes.c_void_p(256)
+    assert lib.awqb_moe_align_ex(p, 32768, 0, 128, 128, p, 32768 + 128 * 127, p, p, p, need - 4, None) == 1
+    assert b"workspace too small" in lib.awqb_last_error()
+    assert lib.awqb_moe_align_ex(p, 32768, 0, 128, 128, p, 100, p, p, p, need, None) == 1  # sorted_ids too small
+    assert lib.awqb_moe_align_ex(p, 32768, 0, 1024, 128, p, 1 << 20, p, p, p, need, None) == 1  # too many experts
+
+
 def test_norm_layers_mirror_reference_interface():
     from sglite_b200.norm import RMSNorm, RMSNormFused
 
