@@ -150,7 +150,8 @@ def test_gemm_data_parallel_waves(cuda, ntok):
     assert ops.device_error() == 0
 
 
-@pytest.mark.parametrize("K,N,M", [(4096, 4096, 1), (4096, 4096, 33), (4096, 4096, 64), (8192, 1280, 5), (1024, 8192, 16)])
+@pytest.mark.parametrize("K,N,M", [(4096, 4096, 1), (4096, 4096, 33), (4096, 4096, 64), (8192, 1280, 5), (1024, 8192, 16),
+                                   (4096, 2560, 256)])
 def test_gemm_cluster_split_k(cuda, K, N, M):
     """Few feature tiles: each tile's stages are split over a thread-block
     cluster and reduced through distributed shared memory. Checked against the
