@@ -81,12 +81,28 @@ int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int 
                  const void* blob, const void* bias, void* y, void* workspace,
                  int64_t workspace_bytes, int ntok, int64_t ctas, void* stream);
 /* The launch awqb_gemm / awqb_gemm_ex would make for these arguments: token
- * tile, CTA count, and cluster size (1 = stream-K with the reduction through
- * the workspace; >= 2 = one tile per cluster of that many CTAs, reduced
- * through distributed shared memory). Diagnostics; no counterpart in the
- * reference. */
+ * tile, CTA count, and cluster size (0 = the small-batch kernel below, one
+ * slice of output features per CTA over all of K; 1 = stream-K with the
+ * reduction through the workspace; >= 2 = one tile per cluster of that many
+ * CTAs, reduced through distributed shared memory). Diagnostics; no
+ * counterpart in the reference. */
 int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t ctas, int* ntok_out,
                    int64_t* ctas_out, int* cluster_out);
+
+/* Small-batch (decode) kernel that awqb_gemm takes for small M (see
+ * awqb_gemm_plan: cluster 0) when no token tile or CTA count is forced: each
+ * CTA computes features_per_cta output features over all of K with `warps`
+ * compute warps, the weights dequantised in registers and multiplied on
+ * mma.sync with fp32 accumulation. Built pairs (features_per_cta, warps):
+ * (16, 16), (32, 16), (32, 8), (64, 8); 0 picks by M, N and the SM count.
+ * ring (1..16, 0 = by shared memory) is its depth of load stages (warps
+ * k-blocks each). 1 <= M <= 16. Needs no workspace. silu_mul != 0 gives the
+ * output of awqb_gemm_silu_mul (interleaved gate/up columns, y [M][N/2]).
+ * Exposed for tuning and tests. Replaces, for decode batches,
+ * awq_gemm_triton, layers/quantization/awq_triton.py:144-195. */
+int awqb_gemv_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                 const void* blob, const void* bias, void* y, int features_per_cta, int warps, int ring,
+                 int silu_mul, void* stream);
 
 /* GEMM for callers that cannot provide or allocate device memory: a host that
  * owns every device byte through its own arena, or code that must never call

@@ -38,6 +38,8 @@ _SIGNATURES = {
         c_int,
         [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp, c_i64, c_int, c_i64, c_vp],
     ),
+    "awqb_gemv_ex": (
+        c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_int, c_int, c_int, c_int, c_vp]),
     "awqb_gemm_noalloc_scratch_bytes": (c_i64, []),
     "awqb_gemm_noalloc": (c_int, [c_vp, c_i64, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp, c_vp]),
     "awqb_moe_topk_softmax": (c_int, [c_vp, c_i64, c_i64, c_i64, c_int, c_vp, c_vp, c_vp]),

@@ -13,6 +13,7 @@
 #include "awqb200.h"
 #include "awqb_common.h"
 #include "awqb_gemm.cuh"
+#include "awqb_gemv.cuh"
 
 namespace awqb {
 
@@ -336,6 +337,257 @@ struct TpExchange {
   }
 };
 
+// ---------------------------------------------------------------------------
+// Small-batch path (awqb_gemv.cuh): M <= kGemvMaxM, no workspace.
+constexpr int kGemvMaxM = 16;
+
+// Whether awqb_gemm takes the small-batch kernel: up to 16 rows, except wide
+// outputs above 8 rows, where the tcgen05 kernel was measured faster
+// (gate_up 4096 -> 28672 at M = 12 / 16: 21.1 vs 25.6 us).
+bool gemv_takes(int64_t M, int64_t N) { return M >= 1 && M <= kGemvMaxM && !(N >= 16384 && M > 8); }
+
+struct GemvPlan {
+  int F = 0, MT = 0, W = 0, ring = 0, stages = 0, kb_real = 0, gpb = 1;
+  int64_t ctas = 0;
+  int64_t smem = 0;
+};
+
+template <int F, int MT, int GPB, int W>
+int64_t gemv_stage_bytes(int M) { return GemvCfg<F, MT, GPB, W>::stage_bytes(M); }
+
+// Stage size of a built configuration (0 if not built). It does not depend on
+// MT.
+int64_t gemv_stage_bytes_rt(int F, int W, int gpb, int M) {
+  switch ((F * 32 + W) * 8 + gpb) {
+#define AWQB_SB(f, w, g) \
+  case ((f) * 32 + (w)) * 8 + (g): return gemv_stage_bytes<f, 8, g, w>(M);
+    AWQB_SB(16, 16, 1) AWQB_SB(16, 16, 2) AWQB_SB(16, 16, 4)
+    AWQB_SB(32, 16, 1) AWQB_SB(32, 16, 2) AWQB_SB(32, 16, 4)
+    AWQB_SB(32, 8, 1) AWQB_SB(32, 8, 2) AWQB_SB(32, 8, 4)
+    AWQB_SB(64, 8, 1) AWQB_SB(64, 8, 2) AWQB_SB(64, 8, 4)
+#undef AWQB_SB
+  }
+  return 0;
+}
+
+bool gemv_built(int F, int W) { return (W == 16 && (F == 16 || F == 32)) || (W == 8 && (F == 32 || F == 64)); }
+
+// Shared memory one SM gives a GEMV launch's CTAs when several share it (about
+// half of the SM, so that the next kernel's CTAs can start beside them and
+// prefetch their weights under programmatic dependent launch); a launch with
+// one CTA per SM may use more.
+constexpr int64_t kGemvSmemPerSm = 110 * 1024;
+constexpr int64_t kGemvSmemAlone = 160 * 1024;
+constexpr int64_t kGemvSmemFixed = 1024 + 256;  // alignment slack + barriers
+
+// Configuration, from sweeps on B200 over the Llama-3-8B decode projections
+// (M = 1..16, every built slice / warp count / ring depth):
+//  * outputs of at least 16384 features: 8 warps, 32-feature slices (many
+//    CTAs, two or three per SM);
+//  * 8 or more rows and at least 6144 features: 8 warps, 64-feature slices
+//    (the activation tile is read once per 64 features);
+//  * more than 8 rows otherwise: 8 warps, 32-feature slices;
+//  * up to 8 rows otherwise: 16 warps per CTA (few CTAs: more warps per SM),
+//    with 16-feature slices for up to 4 rows over K <= 4096 and 32 otherwise.
+// ring = shared-memory stages: as many as the budget allows once the CTAs are
+// spread over the SMs.
+int gemv_plan(int64_t M, int64_t K, int64_t N, int64_t G, int F_req, int W_req, int ring_req, GemvPlan* gp) {
+  AWQB_REQUIRE(M >= 1 && M <= kGemvMaxM, kInvalidArgument, "small-batch path takes 1..%d rows (M=%lld)",
+               kGemvMaxM, (long long)M);
+  AWQB_REQUIRE(F_req == 0 || F_req == 16 || F_req == 32 || F_req == 64, kInvalidArgument,
+               "feature slice %d not built (16, 32 or 64)", F_req);
+  AWQB_REQUIRE(W_req == 0 || W_req == 8 || W_req == 16, kInvalidArgument, "compute warps %d not built (8 or 16)",
+               W_req);
+  AWQB_REQUIRE(ring_req >= 0 && ring_req <= 16, kInvalidArgument, "ring depth %d out of range (1..16, 0 = default)",
+               ring_req);
+  const int sm = device_sm_count();
+  gp->MT = M <= 8 ? 8 : 16;
+  gp->gpb = groups_per_block((int)G);
+  int W = W_req, F = F_req;
+  if (W == 0 && F == 0) {
+    if (N >= 16384) {
+      W = 8, F = 32;
+    } else if (M >= 8 && N >= 6144) {
+      W = 8, F = 64;
+    } else if (M > 8) {
+      W = 8, F = 32;
+    } else {
+      W = 16;
+      F = (M <= 4 && K <= 4096 && (N + 15) / 16 <= 2 * sm) ? 16 : 32;
+    }
+  }
+  if (W == 0) W = (F == 16) ? 16 : (F == 64) ? 8 : (N >= 16384 || M > 8 ? 8 : 16);
+  if (F == 0) F = (W == 8) ? 32 : ((M <= 4 && K <= 4096 && (N + 15) / 16 <= 2 * sm) ? 16 : 32);
+  AWQB_REQUIRE(gemv_built(F, W), kUnsupported, "small-batch kernel with %d-feature slices and %d warps not built",
+               F, W);
+  const int64_t sb = gemv_stage_bytes_rt(F, W, gp->gpb, (int)M);
+  AWQB_REQUIRE(sb > 0, kUnsupported, "no small-batch kernel for this configuration");
+  AWQB_REQUIRE(kGemvSmemFixed + 2 * sb <= 227 * 1024 || (F_req > 0 && ring_req == 1), kUnsupported,
+               "small-batch stages of %lld bytes do not fit twice in shared memory", (long long)sb);
+  gp->F = F;
+  gp->W = W;
+  gp->ctas = (N + F - 1) / F;
+  gp->kb_real = (int)((K + kBlockK - 1) / kBlockK);
+  gp->stages = (gp->kb_real + W - 1) / W;
+  if (ring_req > 0) {
+    gp->ring = ring_req;
+  } else {
+    const int64_t per_sm = (gp->ctas + sm - 1) / sm;
+    const int64_t budget = per_sm == 1 ? kGemvSmemAlone : kGemvSmemPerSm / per_sm;
+    int64_t r = (budget - kGemvSmemFixed) / sb;
+    r = std::max<int64_t>(2, std::min<int64_t>(16, r));
+    gp->ring = (int)r;
+  }
+  if (gp->ring > gp->stages) gp->ring = std::max(1, gp->stages);
+  // the epilogue's cross-warp reduction reuses the ring
+  const int64_t red = (int64_t)W * F * gp->MT * 4;
+  while ((int64_t)gp->ring * sb < red) ++gp->ring;
+  gp->smem = kGemvSmemFixed + (int64_t)gp->ring * sb;
+  AWQB_REQUIRE(gp->smem <= 227 * 1024, kUnsupported, "small-batch ring of %d stages does not fit (%lld bytes)",
+               gp->ring, (long long)gp->smem);
+  return kOk;
+}
+
+int encode_4d(CUtensorMap* tm, CUtensorMapDataType dt, const void* base, const cuuint64_t (&gdim)[4],
+              const cuuint64_t (&gstride)[3], const cuuint32_t (&box)[4]) {
+  auto enc = tensor_map_encoder();
+  AWQB_REQUIRE(enc != nullptr, kCudaError, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint32_t estride[4] = {1u, 1u, 1u, 1u};
+  CUresult r = enc(tm, dt, 4, const_cast<void*>(base), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  AWQB_REQUIRE(r == CUDA_SUCCESS, kCudaError, "cuTensorMapEncodeTiled (weights) failed (%d)", (int)r);
+  return kOk;
+}
+
+// The four tensor maps of one small-batch launch (awqb_gemv.cuh).
+int make_gemv_maps(const void* x, const void* blob, int64_t M, int64_t K, int64_t N, const GemvPlan& gp,
+                   CUtensorMap* tw, CUtensorMap* ts, CUtensorMap* tz, CUtensorMap* tx) {
+  const int64_t KB = blob_kblocks(K);
+  const int64_t NT = (N + kBlockN - 1) / kBlockN;
+  const int64_t BB = block_bytes_for_gpb(gp.gpb);
+  const uint8_t* b = static_cast<const uint8_t*>(blob);
+  const int zw = gp.F / 8 < 4 ? 4 : gp.F / 8;
+  {
+    const cuuint64_t gdim[4] = {512, 4, (cuuint64_t)KB, (cuuint64_t)NT};
+    const cuuint64_t gstr[3] = {2048, (cuuint64_t)BB, (cuuint64_t)(KB * BB)};
+    const cuuint32_t box[4] = {(cuuint32_t)(4 * gp.F), 4, (cuuint32_t)gp.W, 1};
+    int st = encode_4d(tw, CU_TENSOR_MAP_DATA_TYPE_UINT32, b, gdim, gstr, box);
+    if (st != kOk) return st;
+  }
+  {
+    const cuuint64_t gdim[4] = {128, (cuuint64_t)gp.gpb, (cuuint64_t)KB, (cuuint64_t)NT};
+    const cuuint64_t gstr[3] = {256, (cuuint64_t)BB, (cuuint64_t)(KB * BB)};
+    const cuuint32_t box[4] = {(cuuint32_t)gp.F, (cuuint32_t)gp.gpb, (cuuint32_t)gp.W, 1};
+    int st = encode_4d(ts, CU_TENSOR_MAP_DATA_TYPE_UINT16, b + scale_off(), gdim, gstr, box);
+    if (st != kOk) return st;
+  }
+  {
+    const cuuint64_t gdim[4] = {16, (cuuint64_t)gp.gpb, (cuuint64_t)KB, (cuuint64_t)NT};
+    const cuuint64_t gstr[3] = {64, (cuuint64_t)BB, (cuuint64_t)(KB * BB)};
+    const cuuint32_t box[4] = {(cuuint32_t)zw, (cuuint32_t)gp.gpb, (cuuint32_t)gp.W, 1};
+    int st = encode_4d(tz, CU_TENSOR_MAP_DATA_TYPE_UINT32, b + zero_off(gp.gpb), gdim, gstr, box);
+    if (st != kOk) return st;
+  }
+  {
+    auto enc = tensor_map_encoder();
+    AWQB_REQUIRE(enc != nullptr, kCudaError, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t gdim[3] = {32, (cuuint64_t)M, (cuuint64_t)(K / 32)};
+    const cuuint64_t gstr[2] = {(cuuint64_t)K * 2, 64};
+    const cuuint32_t box[3] = {32, (cuuint32_t)M, (cuuint32_t)(4 * gp.W)};
+    const cuuint32_t estride[3] = {1u, 1u, 1u};
+    CUresult r = enc(tx, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(x), gdim, gstr, box, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AWQB_REQUIRE(r == CUDA_SUCCESS, kCudaError, "cuTensorMapEncodeTiled (activations) failed (%d)", (int)r);
+  }
+  return kOk;
+}
+
+template <typename T, int F, int MT, int GPB, int W>
+int gemv_launch_t(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz, const CUtensorMap& tx,
+                  const GemvParams& p, const GemvPlan& gp, cudaStream_t stream) {
+  using Cfg = GemvCfg<F, MT, GPB, W>;
+  auto kern = awq_gemv_kernel<T, F, MT, GPB, W>;
+  static bool attr_set[kMaxDevices] = {};
+  int dev = 0;
+  AWQB_CUDA(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < kMaxDevices && !attr_set[dev]) {
+    AWQB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)gp.ctas);
+  cfg.blockDim = dim3(Cfg::kThreads);
+  cfg.dynamicSmemBytes = (size_t)gp.smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  AWQB_CUDA(cudaLaunchKernelEx(&cfg, kern, tw, ts, tz, tx, p));
+  return kOk;
+}
+
+template <typename T, int F, int MT, int W>
+int gemv_launch_g(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz, const CUtensorMap& tx,
+                  const GemvParams& p, const GemvPlan& gp, cudaStream_t s) {
+  switch (gp.gpb) {
+    case 1: return gemv_launch_t<T, F, MT, 1, W>(tw, ts, tz, tx, p, gp, s);
+    case 2: return gemv_launch_t<T, F, MT, 2, W>(tw, ts, tz, tx, p, gp, s);
+    case 4: return gemv_launch_t<T, F, MT, 4, W>(tw, ts, tz, tx, p, gp, s);
+  }
+  AWQB_REQUIRE(false, kUnsupported, "groups per block %d not built", gp.gpb);
+  return kUnsupported;
+}
+
+template <typename T, int MT>
+int gemv_launch_m(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz, const CUtensorMap& tx,
+                  const GemvParams& p, const GemvPlan& gp, cudaStream_t s) {
+  if (gp.W == 16 && gp.F == 16) return gemv_launch_g<T, 16, MT, 16>(tw, ts, tz, tx, p, gp, s);
+  if (gp.W == 16 && gp.F == 32) return gemv_launch_g<T, 32, MT, 16>(tw, ts, tz, tx, p, gp, s);
+  if (gp.W == 8 && gp.F == 32) return gemv_launch_g<T, 32, MT, 8>(tw, ts, tz, tx, p, gp, s);
+  if (gp.W == 8 && gp.F == 64) return gemv_launch_g<T, 64, MT, 8>(tw, ts, tz, tx, p, gp, s);
+  AWQB_REQUIRE(false, kUnsupported, "small-batch kernel F=%d W=%d not built", gp.F, gp.W);
+  return kUnsupported;
+}
+
+template <typename T>
+int gemv_launch(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz, const CUtensorMap& tx,
+                const GemvParams& p, const GemvPlan& gp, cudaStream_t s) {
+  return gp.MT == 8 ? gemv_launch_m<T, 8>(tw, ts, tz, tx, p, gp, s) : gemv_launch_m<T, 16>(tw, ts, tz, tx, p, gp, s);
+}
+
+// y = x * dequant(blob) (+ bias) for 1 <= M <= kGemvMaxM; sizes already
+// validated by make_plan, pointers by the caller.
+int gemv_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype, const void* blob,
+              const void* bias, void* y, int F_req, int W_req, int ring_req, bool silu, void* stream) {
+  GemvPlan gp;
+  int st = gemv_plan(M, K, N, G, F_req, W_req, ring_req, &gp);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(K % 32 == 0, kUnsupported, "K=%lld must be a multiple of 32", (long long)K);
+  uint32_t* err = device_err_ptr();
+  AWQB_REQUIRE(err != nullptr, kCudaError, "cannot resolve the device error word");
+  CUtensorMap tw, ts, tz, tx;
+  st = make_gemv_maps(x, blob, M, K, N, gp, &tw, &ts, &tz, &tx);
+  if (st != kOk) return st;
+  GemvParams p{};
+  p.bias = bias;
+  p.y = y;
+  p.ldy = silu ? N / 2 : N;
+  p.M = (int32_t)M;
+  p.N = (int32_t)N;
+  p.K = (int32_t)K;
+  p.kb_real = gp.kb_real;
+  p.stages = gp.stages;
+  p.ring = gp.ring;
+  p.silu_mul = silu ? 1 : 0;
+  p.err = err;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == AWQB_DTYPE_F16) return gemv_launch<__half>(tw, ts, tz, tx, p, gp, s);
+  return gemv_launch<__nv_bfloat16>(tw, ts, tz, tx, p, gp, s);
+}
+
 int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
               const void* blob, const void* bias, void* y, void* workspace,
               int64_t workspace_bytes, int ntok, int64_t ctas, void* stream,
@@ -352,6 +604,10 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
   AWQB_REQUIRE(((uintptr_t)x & 15) == 0, kInvalidArgument, "x must be 16-byte aligned");
   AWQB_REQUIRE(((uintptr_t)blob & 15) == 0, kInvalidArgument, "blob must be 16-byte aligned");
+  // Decode batches take the small-batch kernel (no workspace) unless a token
+  // tile or CTA count was forced, or the call is the fused all-reduce.
+  if (tp == nullptr && ntok == 0 && ctas <= 0 && gemv_takes(M, N))
+    return gemv_impl(x, M, K, N, G, dtype, blob, bias, y, 0, 0, 0, silu, stream);
   AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
                "workspace must be non-null and 256-byte aligned");
   AWQB_REQUIRE(workspace_bytes >= pl.cnt_bytes + pl.part_bytes, kInvalidArgument,
@@ -445,6 +701,15 @@ extern "C" int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int nt
   if (st != kOk) return st;
   AWQB_REQUIRE(ntok_out != nullptr && ctas_out != nullptr && cluster_out != nullptr, kInvalidArgument,
                "null output pointer");
+  if (ntok == 0 && ctas <= 0 && gemv_takes(M, N)) {
+    GemvPlan gp;
+    st = gemv_plan(M, K, N, G, 0, 0, 0, &gp);
+    if (st != kOk) return st;
+    *ntok_out = gp.MT;
+    *ctas_out = gp.ctas;
+    *cluster_out = 0;
+    return kOk;
+  }
   *ntok_out = pl.ntok;
   *ctas_out = pl.ctas;
   *cluster_out = pl.cluster_s;
@@ -469,6 +734,21 @@ extern "C" int awqb_gemm_ex(const void* x, int64_t M, int64_t K, int64_t N, int6
                             int64_t workspace_bytes, int ntok, int64_t ctas, void* stream) {
   return gemm_impl(x, M, K, N, G, dtype, blob, bias, y, workspace, workspace_bytes, ntok, ctas,
                    stream);
+}
+
+extern "C" int awqb_gemv_ex(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
+                            const void* blob, const void* bias, void* y, int features_per_cta, int warps, int ring,
+                            int silu_mul, void* stream) {
+  Plan pl;
+  int st = make_plan(M, K, N, G, 0, 0, &pl, false);
+  if (st != kOk) return st;
+  AWQB_REQUIRE(dtype == AWQB_DTYPE_F16 || dtype == AWQB_DTYPE_BF16, kInvalidArgument,
+               "dtype %d is not fp16 (0) or bf16 (1)", dtype);
+  AWQB_REQUIRE(!silu_mul || N % 16 == 0, kInvalidArgument, "fused SiLU-and-mul needs N %% 16 == 0");
+  AWQB_REQUIRE(x != nullptr && blob != nullptr && y != nullptr, kInvalidArgument, "null pointer");
+  AWQB_REQUIRE(((uintptr_t)x & 15) == 0 && ((uintptr_t)blob & 15) == 0, kInvalidArgument,
+               "x and blob must be 16-byte aligned");
+  return gemv_impl(x, M, K, N, G, dtype, blob, bias, y, features_per_cta, warps, ring, silu_mul != 0, stream);
 }
 
 // ---------------------------------------------------------------------------

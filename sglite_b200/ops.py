@@ -137,9 +137,17 @@ class _WorkspacePool:
     """One zero-filled scratch buffer per device, grown on demand.
 
     The GEMM keeps its split-tile counters in the first 8 KiB of any workspace
-    and leaves them at zero after every call, so the buffer is zeroed only when
-    it is (re)allocated; the rest is scratch shared by calls of every shape. Growing is refused while a CUDA graph
-    is being captured: size it first (``reserve``) with the largest call.
+    and leaves them at zero after every call that completes, so the buffer is
+    zeroed only when it is (re)allocated; the rest is scratch shared by calls of
+    every shape. A call whose bounded device wait gave up (``device_error``
+    non-zero) can leave counters set: ``clear_device_error`` zeroes the counter
+    region of every pool buffer together with the error word.
+
+    One buffer serves every stream of a device, so pool-backed calls must not
+    run concurrently on different streams (they would share counters and
+    partial tiles); pass ``workspace=`` to give concurrent streams their own.
+    Growing is refused while a CUDA graph is being captured: size it first
+    (``reserve``) with the largest call.
     """
 
     def __init__(self):
@@ -166,6 +174,18 @@ class _WorkspacePool:
     def reserve(self, device: torch.device, nbytes: int) -> None:
         self.get(device, nbytes)
 
+    def reset_counters(self) -> None:
+        """Zero the split-tile counter region of every buffer (on each
+        device's current stream)."""
+        with self._lock:
+            for idx, buf in self._bufs.items():
+                with torch.cuda.device(idx):
+                    buf[:COUNTER_BYTES].zero_()
+
+
+# Split-tile counters at the start of every GEMM workspace (two int32 per CTA,
+# at most 1024 CTAs): kCounterBytes in awqb_gemm.cu.
+COUNTER_BYTES = 8192
 
 workspace_pool = _WorkspacePool()
 
@@ -235,6 +255,29 @@ def gemm(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
     return out if x.dim() == 2 else out.reshape(*x.shape[:-1], N)
 
 
+def gemv(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int, bias: Optional[torch.Tensor] = None,
+         out: Optional[torch.Tensor] = None, features_per_cta: int = 0, warps: int = 0, ring: int = 0,
+         silu_mul: bool = False) -> torch.Tensor:
+    """The small-batch kernel (1 <= M <= 16) with an explicit feature slice per
+    CTA and compute-warp count ((16, 16), (32, 16), (32, 8) or (64, 8); 0 =
+    default) and ring depth (1..16; 0 = default). ``gemm`` takes it by itself
+    for small M; this entry point exists for tuning and tests. silu_mul:
+    interleaved gate/up blob, output [M, N/2]."""
+    x2 = x.reshape(-1, K).contiguous()
+    M = x2.shape[0]
+    dev = _check_cuda(x2, blob)
+    n_out = N // 2 if silu_mul else N
+    if out is None:
+        out = torch.empty((M, n_out), dtype=x.dtype, device=dev)
+    with _DeviceGuard(dev):
+        call("awqb_gemv_ex", _p(x2), M, K, N, G, _dtype_code(x.dtype), _p(blob), _p(bias), _p(out),
+             int(features_per_cta), int(warps), int(ring), int(bool(silu_mul)), _stream(dev))
+    return out.reshape(*x.shape[:-1], n_out)
+
+
+GEMV_MAX_M = 16  # awqb_gemm takes the small-batch kernel up to this many rows
+
+
 _GEMM_EX = None
 
 
@@ -246,12 +289,23 @@ def _gemm_ex():
 
 
 def device_error(clear: bool = True) -> int:
-    """Bits set by kernels whose bounded waits gave up (synchronises)."""
+    """Bits set by kernels whose bounded waits gave up (synchronises). With
+    clear, a non-zero word is reset by ``clear_device_error``."""
     v = ctypes.c_uint32(0)
     call("awqb_device_error", ctypes.byref(v))
     if clear and v.value:
-        call("awqb_clear_device_error")
+        clear_device_error()
     return v.value
+
+
+def clear_device_error() -> None:
+    """Reset the device error word and the split-tile counters of every pooled
+    workspace: a GEMM that gave up waiting may have left its tile's arrival
+    counters non-zero, which later calls sharing the workspace would take for
+    other contributors' partials. Synchronises the device."""
+    call("awqb_clear_device_error")
+    workspace_pool.reset_counters()
+    torch.cuda.synchronize()
 
 
 def abi_version() -> int:

@@ -157,16 +157,17 @@ def test_gemm_cluster_split_k(cuda, K, N, M):
     cluster and reduced through distributed shared memory. Checked against the
     oracle and against the stream-K launch (reduction through the workspace)."""
     G = 128
-    plan = ops.gemm_plan(M, K, N, G)
+    nt = 16 if M <= 16 else 0  # small M: force the tcgen05 kernel (the default is the small-batch one)
+    plan = ops.gemm_plan(M, K, N, G, ntok=nt)
     assert plan["cluster"] >= 2, plan
     w, x, blob = _setup(cuda, M, K, N, G, torch.bfloat16, seed=K + N + M)
-    y = ops.gemm(x.to(cuda), blob, K, N, G)
+    y = ops.gemm(x.to(cuda), blob, K, N, G, ntok=nt)
     ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
     assert rel_err(y, ref) <= TOL
     y_sk = ops.gemm(x.to(cuda), blob, K, N, G, ctas=torch.cuda.get_device_properties(cuda).multi_processor_count)
     assert ops.gemm_plan(M, K, N, G, ctas=1)["cluster"] == 1
     assert rel_err(y, y_sk.float()) <= TOL
-    assert torch.equal(y, ops.gemm(x.to(cuda), blob, K, N, G))  # deterministic
+    assert torch.equal(y, ops.gemm(x.to(cuda), blob, K, N, G, ntok=nt))  # deterministic
     assert ops.device_error() == 0
 
 
@@ -189,4 +190,28 @@ def test_gemm_silu_mul_fused(cuda, I, M, dtype):
     ref = torch.nn.functional.silu(h[:, :I]) * h[:, I:]
     assert y.shape == (M, I)
     assert rel_err(y, ref) <= TOL
+    assert ops.device_error() == 0
+
+
+def test_clear_device_error_resets_pooled_counters(cuda):
+    """Counters left non-zero in the shared workspace (as a GEMM whose bounded
+    wait gave up may leave them) are zeroed by clear_device_error, after which a
+    split-K GEMM on the pool equals one on a fresh workspace bit for bit."""
+    M, K, N, G = 64, 4096, 14336, 128
+    assert ops.gemm_plan(M, K, N, G)["cluster"] == 1  # stream-K: counters in the workspace
+    w, x, blob = _setup(cuda, M, K, N, G, torch.bfloat16, seed=77)
+    xd = x.to(cuda)
+    ops.gemm(xd, blob, K, N, G)  # sizes the pool
+    torch.cuda.synchronize()
+    for buf in ops.workspace_pool._bufs.values():
+        buf[:ops.COUNTER_BYTES].fill_(0x5A)  # host-side poison; no GEMM runs on it
+    ops.clear_device_error()
+    for buf in ops.workspace_pool._bufs.values():
+        assert int(buf[:ops.COUNTER_BYTES].count_nonzero()) == 0
+    y_pool = ops.gemm(xd, blob, K, N, G)
+    fresh = torch.zeros(ops.gemm_workspace_bytes(M, K, N, G), dtype=torch.uint8, device=cuda)
+    y_fresh = ops.gemm(xd, blob, K, N, G, workspace=fresh)
+    assert torch.equal(y_pool, y_fresh)
+    ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+    assert rel_err(y_pool, ref) <= TOL
     assert ops.device_error() == 0

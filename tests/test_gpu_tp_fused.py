@@ -21,6 +21,14 @@ def exchange(cuda):
     ex.destroy()
 
 
+def _plain(x, blob, K, N, G, bias=None):
+    """The plain GEMM on the kernel the fused call uses (the tcgen05 one; for
+    M <= 16 the default would be the small-batch kernel, whose summation order
+    differs)."""
+    nt = 16 if x.shape[0] <= 16 else 0
+    return ops.gemm(x, blob, K, N, G, bias=bias, ntok=nt)
+
+
 def _blob(cuda, K, N, G, dt, seed):
     w = make_awq_weights(K, N, G, dt, seed=seed)
     return w, ops.repack(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
@@ -36,7 +44,7 @@ def test_fused_equals_plain_gemm(cuda, exchange, K, N, mode):
         for M in (1, 5, 33, 64):
             x = make_activations(M, K, dt, seed=M + rep).to(cuda)
             y = exchange.gemm_allreduce(x, blob, K, N, G)
-            assert torch.equal(y, ops.gemm(x, blob, K, N, G)), (K, N, M, rep, ops.gemm_plan(M, K, N, G))
+            assert torch.equal(y, _plain(x, blob, K, N, G)), (K, N, M, rep, ops.gemm_plan(M, K, N, G))
     x = make_activations(7, K, dt, seed=3)
     ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
     assert rel_err(exchange.gemm_allreduce(x.to(cuda), blob, K, N, G), ref) <= 1e-2
@@ -48,7 +56,7 @@ def test_fused_bias_and_fp16(cuda, exchange):
     _, blob = _blob(cuda, K, N, G, dt, 5)
     bias = torch.randn(N, device=cuda).to(dt)
     x = make_activations(9, K, dt, seed=1).to(cuda)
-    assert torch.equal(exchange.gemm_allreduce(x, blob, K, N, G, bias=bias), ops.gemm(x, blob, K, N, G, bias=bias))
+    assert torch.equal(exchange.gemm_allreduce(x, blob, K, N, G, bias=bias), _plain(x, blob, K, N, G, bias=bias))
     assert ops.device_error() == 0
 
 
@@ -73,7 +81,7 @@ def test_fused_inside_cuda_graph_odd_call_count(cuda, exchange):
         g.replay()
         torch.cuda.synchronize()
         for (K, N), b, x, o in zip(shapes, blobs, xs, outs):
-            assert torch.equal(o, ops.gemm(x, b, K, N, G))
+            assert torch.equal(o, _plain(x, b, K, N, G))
     del g
     assert ops.device_error() == 0
 
@@ -84,3 +92,25 @@ def test_fused_rejects_oversized_batches(cuda, exchange):
     x = make_activations(65, K, torch.bfloat16, seed=1).to(cuda)
     with pytest.raises(ValueError):
         exchange.gemm_allreduce(x, blob, K, N, G)
+
+
+def test_fused_stream_k_epilogue_up_to_256_rows(cuda):
+    """An exchange sized for 256 rows: M = 256 over N = 8192 has more tiles than
+    half the SMs, so the fused all-reduce runs in the stream-K epilogue
+    (tp_put / tp_finish); three calls alternate both landing parities and must
+    equal the plain GEMM of the same plan bit for bit."""
+    G, dt, K, N, M = 128, torch.bfloat16, 1024, 8192, 256
+    ex = init_peer_exchange(tp_rank=0, tp_size=1, tp_cpu_group=None, device=cuda, max_rows=256, max_n=N)
+    try:
+        assert ops.gemm_plan(M, K, N, G)["cluster"] == 1
+        w, blob = _blob(cuda, K, N, G, dt, 11)
+        for rep in range(3):
+            x = make_activations(M, K, dt, seed=rep).to(cuda)
+            y = ex.gemm_allreduce(x, blob, K, N, G)
+            assert torch.equal(y, ops.gemm(x, blob, K, N, G)), rep
+        x = make_activations(M, K, dt, seed=5)
+        ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
+        assert rel_err(ex.gemm_allreduce(x.to(cuda), blob, K, N, G), ref) <= 1e-2
+        assert ops.device_error() == 0
+    finally:
+        ex.destroy()

@@ -13,7 +13,7 @@ import ctypes
 import pytest
 import torch
 
-from oracle.awq_ref import rel_err
+from oracle.awq_ref import awq_linear_ref, dequant_ref, gemm_ref, rel_err
 from sglite_b200 import _lib, ops
 from sglite_b200.synthetic import make_activations, make_awq_weights
 
@@ -38,11 +38,39 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda, M, K, N):
     w = make_awq_weights(K, N, G, torch.bfloat16, seed=M + K)
     blob = ops.repack(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)
     for call in range(2):  # the scratch keeps the previous call's contents
-        x = make_activations(M, K, torch.bfloat16, seed=100 * call + M).to(cuda)
-        ref = ops.gemm(x, blob, K, N, G)
-        y = _noalloc(x, blob, K, N, G, torch.empty((M, N), dtype=torch.bfloat16, device=cuda))
+        x = make_activations(M, K, torch.bfloat16, seed=100 * call + M)
+        xd = x.to(cuda)
+        ref = ops.gemm(xd, blob, K, N, G)
+        y = _noalloc(xd, blob, K, N, G, torch.empty((M, N), dtype=torch.bfloat16, device=cuda))
         torch.cuda.synchronize()
         assert rel_err(y, ref.float()) <= TOL
+        assert rel_err(y, awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)) <= TOL
+    assert ops.device_error() == 0
+
+
+def test_noalloc_stream_k_partials_in_the_scratch(cuda):
+    """Stream-K plans (cluster == 1) write fp32 partial tiles and split-tile
+    counters into the fixed scratch array: two such shapes, alternated twice,
+    must equal the workspace entry point bit for bit (same plan, same
+    reduction order) and the oracle within the GEMM tolerance."""
+    G = 128
+    shapes = [(64, 4096, 14336), (48, 4096, 12288)]
+    setups = []
+    for M, K, N in shapes:
+        assert ops.gemm_plan(M, K, N, G)["cluster"] == 1, (M, K, N, ops.gemm_plan(M, K, N, G))
+        w = make_awq_weights(K, N, G, torch.bfloat16, seed=N)
+        setups.append((w, ops.repack(*(w[k].to(cuda) for k in ("qweight", "qzeros", "scales")), G)))
+    for rep in range(2):
+        for (M, K, N), (w, blob) in zip(shapes, setups):
+            x = make_activations(M, K, torch.bfloat16, seed=rep * 7 + M)
+            xd = x.to(cuda)
+            y = _noalloc(xd, blob, K, N, G, torch.empty((M, N), dtype=torch.bfloat16, device=cuda))
+            torch.cuda.synchronize()
+            assert torch.equal(y, ops.gemm(xd, blob, K, N, G)), (M, K, N, rep)
+            cols = slice(N - 512, N)
+            Wsl = dequant_ref(w["qweight"][:, (N - 512) // 8:], w["qzeros"][:, (N - 512) // 8:],
+                              w["scales"][:, cols], G)
+            assert rel_err(y[:, cols], gemm_ref(x, Wsl)) <= TOL
     assert ops.device_error() == 0
 
 
