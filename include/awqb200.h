@@ -96,7 +96,7 @@ int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int ntok, int64_t
  * mma.sync with fp32 accumulation. Built pairs (features_per_cta, warps):
  * (16, 16), (32, 16), (32, 8), (64, 8); 0 picks by M, N and the SM count.
  * ring (1..16, 0 = by shared memory) is its depth of load stages (warps
- * k-blocks each). 1 <= M <= 16. Needs no workspace. silu_mul != 0 gives the
+ * k-blocks each). 1 <= M <= 32. Needs no workspace. silu_mul != 0 gives the
  * output of awqb_gemm_silu_mul (interleaved gate/up columns, y [M][N/2]).
  * Exposed for tuning and tests. Replaces, for decode batches,
  * awq_gemm_triton, layers/quantization/awq_triton.py:144-195. */

@@ -339,12 +339,20 @@ struct TpExchange {
 
 // ---------------------------------------------------------------------------
 // Small-batch path (awqb_gemv.cuh): M <= kGemvMaxM, no workspace.
-constexpr int kGemvMaxM = 16;
+constexpr int kGemvMaxM = 32;
 
-// Whether awqb_gemm takes the small-batch kernel: up to 16 rows, except wide
-// outputs above 8 rows, where the tcgen05 kernel was measured faster
-// (gate_up 4096 -> 28672 at M = 12 / 16: 21.1 vs 25.6 us).
-bool gemv_takes(int64_t M, int64_t N) { return M >= 1 && M <= kGemvMaxM && !(N >= 16384 && M > 8); }
+// Whether awqb_gemm takes the small-batch kernel (measured against the
+// tcgen05 kernel on B200 over the Llama-3-8B decode projections): up to 8 rows
+// always; up to 16 rows unless the output is wide (N >= 16384: gate_up at
+// M = 12 / 16, 21.1 vs 25.6 us) or K long (K > 8192: down at M = 16, 14.2 vs
+// 14.4 us); up to 32 rows for problems of at most 16 Mi weights (O 4096 x 4096
+// at M = 32: 8.3 vs 8.7 us). Above, the tcgen05 kernel's larger MMAs win.
+bool gemv_takes(int64_t M, int64_t K, int64_t N) {
+  if (M < 1 || M > kGemvMaxM) return false;
+  if (M <= 8) return true;
+  if (M <= 16) return N < 16384 && K <= 8192;
+  return K * N <= (16ll << 20);
+}
 
 struct GemvPlan {
   int F = 0, MT = 0, W = 0, ring = 0, stages = 0, kb_real = 0, gpb = 1;
@@ -401,13 +409,13 @@ int gemv_plan(int64_t M, int64_t K, int64_t N, int64_t G, int F_req, int W_req, 
   AWQB_REQUIRE(ring_req >= 0 && ring_req <= 16, kInvalidArgument, "ring depth %d out of range (1..16, 0 = default)",
                ring_req);
   const int sm = device_sm_count();
-  gp->MT = M <= 8 ? 8 : 16;
+  gp->MT = M <= 8 ? 8 : M <= 16 ? 16 : 32;
   gp->gpb = groups_per_block((int)G);
   int W = W_req, F = F_req;
   if (W == 0 && F == 0) {
     if (N >= 16384) {
       W = 8, F = 32;
-    } else if (M >= 8 && N >= 6144) {
+    } else if (M >= 8 && M <= 16 && N >= 6144) {
       W = 8, F = 64;
     } else if (M > 8) {
       W = 8, F = 32;
@@ -555,7 +563,9 @@ int gemv_launch_m(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMa
 template <typename T>
 int gemv_launch(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz, const CUtensorMap& tx,
                 const GemvParams& p, const GemvPlan& gp, cudaStream_t s) {
-  return gp.MT == 8 ? gemv_launch_m<T, 8>(tw, ts, tz, tx, p, gp, s) : gemv_launch_m<T, 16>(tw, ts, tz, tx, p, gp, s);
+  if (gp.MT == 8) return gemv_launch_m<T, 8>(tw, ts, tz, tx, p, gp, s);
+  if (gp.MT == 16) return gemv_launch_m<T, 16>(tw, ts, tz, tx, p, gp, s);
+  return gemv_launch_m<T, 32>(tw, ts, tz, tx, p, gp, s);
 }
 
 // y = x * dequant(blob) (+ bias) for 1 <= M <= kGemvMaxM; sizes already
@@ -606,7 +616,7 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   AWQB_REQUIRE(((uintptr_t)blob & 15) == 0, kInvalidArgument, "blob must be 16-byte aligned");
   // Decode batches take the small-batch kernel (no workspace) unless a token
   // tile or CTA count was forced, or the call is the fused all-reduce.
-  if (tp == nullptr && ntok == 0 && ctas <= 0 && gemv_takes(M, N))
+  if (tp == nullptr && ntok == 0 && ctas <= 0 && gemv_takes(M, K, N))
     return gemv_impl(x, M, K, N, G, dtype, blob, bias, y, 0, 0, 0, silu, stream);
   AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
                "workspace must be non-null and 256-byte aligned");
@@ -701,7 +711,7 @@ extern "C" int awqb_gemm_plan(int64_t M, int64_t K, int64_t N, int64_t G, int nt
   if (st != kOk) return st;
   AWQB_REQUIRE(ntok_out != nullptr && ctas_out != nullptr && cluster_out != nullptr, kInvalidArgument,
                "null output pointer");
-  if (ntok == 0 && ctas <= 0 && gemv_takes(M, N)) {
+  if (ntok == 0 && ctas <= 0 && gemv_takes(M, K, N)) {
     GemvPlan gp;
     st = gemv_plan(M, K, N, G, 0, 0, 0, &gp);
     if (st != kOk) return st;

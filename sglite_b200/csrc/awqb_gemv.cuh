@@ -1,11 +1,11 @@
 // Small-batch (decode) W4A16 GEMM for sm_100a: y[M, N] = x[M, K] * dequant(blob)
-// for M <= 16, streaming the weights at HBM speed.
+// for M <= 32, streaming the weights at HBM speed.
 //
 // Replaces, for decode batches, the reference's awq_gemm_kernel with its
 // SPLIT_K = 8 buffer and the .sum(0) pass (layers/quantization/awq_triton.py:
 // 16-136, 173-193) and gptq_marlin_gemm (marlin_utils.py:388-410).
 //
-// Why a second kernel next to the tcgen05 GEMM: at M <= 16 a 128-feature x
+// Why a second kernel next to the tcgen05 GEMM: at small M a 128-feature x
 // 16-token tcgen05.mma multiplies mostly padding, its A operand has to pass
 // through tensor memory (4 bytes of tcgen05.st per int4 weight), and the few
 // 128-feature tiles force a cross-CTA split-K reduction. Here each CTA owns a
@@ -89,7 +89,7 @@ struct GemvCfg {
   __host__ __device__ static constexpr int stage_bytes(int M) { return kXOff + r128(x_bytes(M)); }
   static constexpr int kRedBytes = kWarps * F * MT * 4;  // cross-warp reduction (reuses the ring)
   static_assert(F % 16 == 0 && F >= 16 && F <= 64, "feature slice is 16, 32 or 64");
-  static_assert(MT == 8 || MT == 16, "8 or 16 tokens");
+  static_assert(MT == 8 || MT == 16 || MT == 32, "8, 16 or 32 tokens");
   static_assert(GPB == 1 || GPB == 2 || GPB == 4, "groups per block");
   static_assert(W == 8 || W == 16, "8 or 16 compute warps");
 };

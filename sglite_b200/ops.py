@@ -258,7 +258,7 @@ def gemm(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int,
 def gemv(x: torch.Tensor, blob: torch.Tensor, K: int, N: int, G: int, bias: Optional[torch.Tensor] = None,
          out: Optional[torch.Tensor] = None, features_per_cta: int = 0, warps: int = 0, ring: int = 0,
          silu_mul: bool = False) -> torch.Tensor:
-    """The small-batch kernel (1 <= M <= 16) with an explicit feature slice per
+    """The small-batch kernel (1 <= M <= 32) with an explicit feature slice per
     CTA and compute-warp count ((16, 16), (32, 16), (32, 8) or (64, 8); 0 =
     default) and ring depth (1..16; 0 = default). ``gemm`` takes it by itself
     for small M; this entry point exists for tuning and tests. silu_mul:

@@ -62,8 +62,8 @@ def test_gemm_rejects_bad_arguments_without_touching_the_gpu():
     assert lib.awqb_gemm(ctypes.c_void_p(8), 1, 4096, 4096, 128, 1, ctypes.c_void_p(256), None,
                          ctypes.c_void_p(256), ctypes.c_void_p(256), 1 << 30, None) == 1
     assert b"16-byte" in lib.awqb_last_error()
-    # workspace too small (M > 16: the tcgen05 kernel, which needs one)
-    assert lib.awqb_gemm(ctypes.c_void_p(256), 17, 4096, 4096, 128, 1, ctypes.c_void_p(256), None,
+    # workspace too small (M > 32: the tcgen05 kernel, which needs one)
+    assert lib.awqb_gemm(ctypes.c_void_p(256), 33, 4096, 4096, 128, 1, ctypes.c_void_p(256), None,
                          ctypes.c_void_p(256), ctypes.c_void_p(256), 64, None) == 1
     assert b"workspace too small" in lib.awqb_last_error()
 
@@ -76,8 +76,8 @@ def test_gemv_rejects_bad_arguments_without_touching_the_gpu():
     assert b"feature slice" in lib.awqb_last_error()
     assert lib.awqb_gemv_ex(p, 4, 4096, 4096, 128, 1, p, None, p, 0, 12, 0, 0, None) == 1
     assert lib.awqb_gemv_ex(p, 4, 4096, 4096, 128, 1, p, None, p, 0, 0, 17, 0, None) == 1
-    assert lib.awqb_gemv_ex(p, 17, 4096, 4096, 128, 1, p, None, p, 0, 0, 0, 0, None) == 1
-    assert b"1..16 rows" in lib.awqb_last_error()
+    assert lib.awqb_gemv_ex(p, 33, 4096, 4096, 128, 1, p, None, p, 0, 0, 0, 0, None) == 1
+    assert b"1..32 rows" in lib.awqb_last_error()
     assert lib.awqb_gemv_ex(p, 4, 4096, 4096, 128, 1, p, None, p, 64, 16, 0, 0, None) == 2
     # SiLU-and-mul needs N % 16 == 0; misaligned activations; bad group size
     assert lib.awqb_gemv_ex(p, 4, 4096, 4104, 128, 1, p, None, p, 0, 0, 0, 1, None) == 1

@@ -26,10 +26,12 @@ FW = [(16, 16), (32, 16), (32, 8), (64, 8)]  # built (feature slice, compute war
 
 
 @pytest.mark.parametrize("F,W", FW)
-@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16, 17, 32])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_gemv_slices_and_rows(cuda, F, W, M, dtype):
     K, N, G = 4096, 384, 128
+    if 2 * (W * 4 * M * 64 + W * 4 * F * 16 + 1024) + 1280 > 227 * 1024:
+        pytest.skip("two load stages of this configuration exceed shared memory (rejected by the plan)")
     w, x, blob = _setup(cuda, M, K, N, G, dtype, seed=F + W + M)
     y = ops.gemv(x.to(cuda), blob, K, N, G, features_per_cta=F, warps=W)
     ref = awq_linear_ref(x, w["qweight"], w["qzeros"], w["scales"], G)
