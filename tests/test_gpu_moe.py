@@ -123,3 +123,44 @@ def test_silu_and_mul_layouts(cuda, interleaved):
     plain = torch.cat([h[:, 0::2], h[:, 1::2]], dim=1) if interleaved else h
     out = ops.silu_and_mul(h.to(cuda), interleaved=interleaved)
     assert torch.allclose(out.float().cpu(), silu_and_mul_ref(plain).float(), rtol=1e-2, atol=1e-2)
+
+
+def test_awq_moe_layer_from_a_checkpoint_against_the_oracle(cuda):
+    """The wiring end to end: a synthetic AWQ MoE checkpoint stacked by the
+    restated loader rules, loaded into the AWQ MoE layer, repacked, and run
+    against the oracle's MoE restatement; then the same experts split over two
+    expert-parallel layers (one process), whose summed outputs must match."""
+    from oracle.awq_ref import moe_ref, rel_err
+    from sglite_b200.moe import AWQMoELayer, stack_awq_experts
+    from sglite_b200.quantization import AWQB200Config
+    from sglite_b200.synthetic import make_activations, make_awq_weights, make_router_logits
+
+    E, k, H, I, G, M = 8, 2, 512, 256, 128, 40
+    prefix = "model.layers.3.mlp.experts"
+    ck = {}
+    for e in range(E):
+        for proj, (K, N) in (("gate_proj", (H, I)), ("up_proj", (H, I)), ("down_proj", (I, H))):
+            for kk, v in make_awq_weights(K, N, G, torch.bfloat16, seed=7 * e + len(proj)).items():
+                ck[f"{prefix}.{e}.{proj}.{kk}"] = v
+    st = stack_awq_experts(ck, E)
+    cfg = AWQB200Config(4, G, True)
+    x = make_activations(M, H, torch.bfloat16, seed=1)
+    logits = make_router_logits(M, E, seed=2)
+    w1 = {kk: st[f"{prefix}.gate_up_proj.{kk}"] for kk in ("qweight", "qzeros", "scales")}
+    w2 = {kk: st[f"{prefix}.down_proj.{kk}"] for kk in ("qweight", "qzeros", "scales")}
+    ref = moe_ref(x, w1, w2, logits, k, True, G)
+
+    layer = AWQMoELayer(E, k, H, I, cfg)
+    layer.load_state_dict({kk: v.to(cuda) for kk, v in st.items()}, prefix=prefix)
+    layer.process_weights_after_loading()
+    y = layer.forward(x.to(cuda).clone(), logits.to(cuda))
+    assert rel_err(y, ref) <= 1e-2
+
+    parts = []
+    for r in range(2):
+        lr = AWQMoELayer(E, k, H, I, cfg, ep_rank=r, ep_size=2)
+        lr.load_state_dict({kk: v.to(cuda) for kk, v in st.items()}, prefix=prefix)
+        lr.process_weights_after_loading()
+        parts.append(lr.forward(x.to(cuda).clone(), logits.to(cuda)).float())
+    assert rel_err(parts[0] + parts[1], ref) <= 1e-2
+    assert ops.device_error() == 0
