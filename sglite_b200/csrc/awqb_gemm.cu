@@ -570,8 +570,12 @@ int gemv_launch(const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap&
 
 // y = x * dequant(blob) (+ bias) for 1 <= M <= kGemvMaxM; sizes already
 // validated by make_plan, pointers by the caller.
+struct TpExchange;
+void gemv_set_tp(GemvParams* p, const TpExchange* tp, int64_t M, int64_t N);
+
 int gemv_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype, const void* blob,
-              const void* bias, void* y, int F_req, int W_req, int ring_req, bool silu, void* stream) {
+              const void* bias, void* y, int F_req, int W_req, int ring_req, bool silu, void* stream,
+              const TpExchange* tp = nullptr) {
   GemvPlan gp;
   int st = gemv_plan(M, K, N, G, F_req, W_req, ring_req, &gp);
   if (st != kOk) return st;
@@ -593,9 +597,31 @@ int gemv_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   p.ring = gp.ring;
   p.silu_mul = silu ? 1 : 0;
   p.err = err;
+  if (tp != nullptr) gemv_set_tp(&p, tp, M, N);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return gemv_launch<__half>(tw, ts, tz, tx, p, gp, s);
   return gemv_launch<__nv_bfloat16>(tw, ts, tz, tx, p, gp, s);
+}
+
+// Reduce-scatter + all-gather once the all-to-all traffic (world x the
+// result, in 8-byte words) outweighs the extra hop: from 4 ranks and 8 rows.
+bool tp_use_rsag(const TpExchange* tp, int64_t M) {
+  return tp->mode == 2 || (tp->mode == 0 && tp->world >= 4 && M >= 8);
+}
+
+void gemv_set_tp(GemvParams* p, const TpExchange* tp, int64_t M, int64_t N) {
+  p->tp_world = tp->world;
+  p->tp_rank = tp->rank;
+  p->tp_rows = (int32_t)tp->rows;
+  p->tp_half = tp->half_words;
+  p->tp_fhalf = tp->final_half;
+  for (int r = 0; r < tp->world; ++r) {
+    p->tp_land[r] = tp->land(r);
+    p->tp_final[r] = tp->final_words(r);
+  }
+  p->tp_epoch = tp->epoch();
+  p->tp_rsag = tp_use_rsag(tp, M) ? 1 : 0;
+  (void)N;
 }
 
 int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dtype,
@@ -616,8 +642,15 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
   AWQB_REQUIRE(((uintptr_t)blob & 15) == 0, kInvalidArgument, "blob must be 16-byte aligned");
   // Decode batches take the small-batch kernel (no workspace) unless a token
   // tile or CTA count was forced, or the call is the fused all-reduce.
-  if (tp == nullptr && ntok == 0 && ctas <= 0 && gemv_takes(M, K, N))
-    return gemv_impl(x, M, K, N, G, dtype, blob, bias, y, 0, 0, 0, silu, stream);
+  if (ntok == 0 && ctas <= 0 && gemv_takes(M, K, N)) {
+    if (tp != nullptr) {
+      AWQB_REQUIRE(tp->opened, kInvalidArgument, "exchange not opened (awqb_tp_exchange_open)");
+      AWQB_REQUIRE(M <= tp->rows && N <= tp->max_n, kInvalidArgument,
+                   "fused all-reduce sized for M <= %lld, N <= %lld (got M=%lld, N=%lld)", (long long)tp->rows,
+                   (long long)tp->max_n, (long long)M, (long long)N);
+    }
+    return gemv_impl(x, M, K, N, G, dtype, blob, bias, y, 0, 0, 0, silu, stream, tp);
+  }
   AWQB_REQUIRE(workspace != nullptr && ((uintptr_t)workspace & 255) == 0, kInvalidArgument,
                "workspace must be non-null and 256-byte aligned");
   AWQB_REQUIRE(workspace_bytes >= pl.cnt_bytes + pl.part_bytes, kInvalidArgument,
@@ -665,11 +698,8 @@ int gemm_impl(const void* x, int64_t M, int64_t K, int64_t N, int64_t G, int dty
       p.tp_final[r] = tp->final_words(r);
     }
     p.tp_epoch = tp->epoch();
-    // Reduce-scatter + all-gather once the all-to-all traffic (world x the
-    // result, in 8-byte words) outweighs the extra hop: from 4 ranks and 8
-    // rows; implemented in the cluster split-K finale.
-    const bool rsag = tp->mode == 2 || (tp->mode == 0 && tp->world >= 4 && M >= 8);
-    p.tp_rsag = (pl.cluster_s > 1 && rsag) ? 1 : 0;
+    // reduce-scatter + all-gather is implemented in the cluster split-K finale
+    p.tp_rsag = (pl.cluster_s > 1 && tp_use_rsag(tp, M)) ? 1 : 0;
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == AWQB_DTYPE_F16) return launch_n<__half>(tm, p, pl, true, s);

@@ -62,10 +62,21 @@ struct GemvParams {
   int64_t ldy;
   int32_t M, N, K;
   int32_t kb_real;    // k-blocks holding real input features: ceil(K / 128)
-  int32_t stages;     // ceil(kb_real / 8)
+  int32_t stages;     // ceil(kb_real / W)
   int32_t ring;       // shared-memory stages in the ring (1..16)
   int32_t silu_mul;   // interleaved gate/up columns: y[., j] = silu(col 2j) * col 2j+1
   uint32_t* err;
+  // Fused all-reduce across tensor-parallel ranks (tp_world >= 1), the
+  // protocol of the tcgen05 kernel's exchange (awqb_gemm.cuh, GemmParams):
+  // {fp32, call tag} words into every rank's landing buffer (all-to-all) or
+  // into the slice owner's only, whose rounded sums come back as {16-bit
+  // value, 15-bit tag} words (reduce-scatter + all-gather; owner of CTA c's
+  // slice = rank c % world). Sums are taken in rank order on every rank.
+  int32_t tp_world, tp_rank, tp_rows, tp_rsag;
+  int64_t tp_half, tp_fhalf;    // landing / final words per parity half
+  uint2* tp_land[8];
+  uint32_t* tp_final[8];
+  int32_t* tp_epoch;            // call counter (tag = epoch + 1, buffer = epoch & 1) and CTAs done
 };
 
 template <int F, int MT, int GPB, int W>
@@ -204,6 +215,104 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int3
       ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
       "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// Fused all-reduce epilogue of one CTA's slice (compute warps only; red holds
+// the W per-warp partial sums [warp][token][F]). Two passes: every partial
+// goes out first, then each thread waits (bounded) for the words of the values
+// it sent, sums them in rank order, adds the bias once and stores; in
+// reduce-scatter mode non-owners wait for the owner's rounded result instead.
+// The last CTA to finish advances the rank's call counter.
+template <typename T, int F, int MT>
+__device__ __noinline__ void gemv_exchange(const GemvParams& p, const float* red, int f0, int nwarps) {
+  using Tr = GemvTraits<T>;
+  const int nthreads = 32 * nwarps;
+  const int tid = threadIdx.x;
+  const int M = p.M;
+  grid_dep_wait();  // the counter and the landing buffers belong to the previous grid until now
+  const uint32_t epoch = (uint32_t)*reinterpret_cast<const volatile int*>(p.tp_epoch);
+  const int par = (int)(epoch & 1u);
+  const uint32_t tag = epoch + 1u;
+  const uint32_t t16 = (epoch & 0x7fffu) + 1u;
+  const int world = p.tp_world, rank = p.tp_rank;
+  const int owner = (int)(blockIdx.x % (unsigned)world);
+  const bool rsag = p.tp_rsag != 0;
+  const bool recv = rsag && owner != rank;
+  for (int idx = tid; idx < M * F; idx += nthreads) {
+    const int n = idx / F, f = idx % F;
+    const int col = f0 + f;
+    if (col >= p.N) continue;
+    float v = 0.f;
+    for (int w = 0; w < nwarps; ++w) v += red[(w * MT + n) * F + f];
+    const int64_t o = (int64_t)par * p.tp_half + ((int64_t)rank * p.tp_rows + n) * p.N + col;
+    if (rsag)
+      st_tagged_sys(p.tp_land[owner] + o, v, tag);
+    else
+      for (int d = 0; d < world; ++d) st_tagged_sys(p.tp_land[d] + o, v, tag);
+  }
+  uint64_t t0 = 0;
+  bool ok = true;
+  uint16_t* y = static_cast<uint16_t*>(p.y);
+  for (int idx = tid; ok && idx < M * F; idx += nthreads) {
+    const int n = idx / F, f = idx % F;
+    const int col = f0 + f;
+    if (col >= p.N) continue;
+    uint16_t out;
+    if (recv) {
+      const uint32_t* wp = p.tp_final[rank] + (int64_t)par * p.tp_fhalf + (int64_t)n * p.N + col;
+      uint32_t w = ld_word_sys(wp);
+      while ((w >> 16) != t16) {
+        if (t0 == 0) {
+          t0 = globaltimer_ns();
+        } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+          ok = false;
+          break;
+        }
+        w = ld_word_sys(wp);
+      }
+      if (!ok) break;
+      out = (uint16_t)(w & 0xffffu);
+    } else {
+      float v = 0.f;
+      const uint2* land = p.tp_land[rank] + (int64_t)par * p.tp_half;
+      for (int r = 0; ok && r < world; ++r) {
+        const uint2* wp = land + ((int64_t)r * p.tp_rows + n) * p.N + col;
+        uint2 w = ld_tagged_sys(wp);
+        while (w.y != tag) {
+          if (t0 == 0) {
+            t0 = globaltimer_ns();
+          } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
+            ok = false;
+            break;
+          }
+          w = ld_tagged_sys(wp);
+        }
+        v += __uint_as_float(w.x);
+      }
+      if (!ok) break;
+      if (p.bias != nullptr) v += Tr::to_f32(reinterpret_cast<const uint16_t*>(p.bias)[col]);
+      out = Tr::from_f32(v);
+      if (rsag) {
+        const uint32_t w = (uint32_t)out | (t16 << 16);
+        const int64_t fo = (int64_t)par * p.tp_fhalf + (int64_t)n * p.N + col;
+        for (int d = 0; d < world; ++d)
+          if (d != rank) st_word_sys(p.tp_final[d] + fo, w);
+      }
+    }
+    y[(int64_t)n * p.ldy + col] = out;
+  }
+  if (!ok) atomicOr(p.err, 8u);  // kErrWaitEpilogue (awqb_gemm.cuh)
+  named_bar_sync(1, nthreads);
+  if (tid == 0) {
+    // The last CTA to finish advances this rank's call counter (the parity of
+    // the next fused call); the next kernel reads it after the grid boundary.
+    __threadfence();
+    if (atomicAdd(p.tp_epoch + 1, 1) == (int)gridDim.x - 1) {
+      p.tp_epoch[1] = 0;
+      __threadfence();
+      atomicAdd(p.tp_epoch, 1);
+    }
+  }
 }
 
 // Tensor maps (built on the host, awqb_gemm.cu):
@@ -437,6 +546,10 @@ awq_gemv_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   const T* bias = static_cast<const T*>(p.bias);
   uint16_t* y = static_cast<uint16_t*>(p.y);
   const int tid = threadIdx.x;
+  if (p.tp_world > 0) {
+    gemv_exchange<T, F, MT>(p, red, f0, Cfg::kWarps);
+    return;
+  }
   if (!p.silu_mul) {
     for (int idx = tid; idx < M * F; idx += 32 * Cfg::kWarps) {
       const int n = idx / F, f = idx % F;

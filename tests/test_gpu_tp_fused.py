@@ -22,11 +22,10 @@ def exchange(cuda):
 
 
 def _plain(x, blob, K, N, G, bias=None):
-    """The plain GEMM on the kernel the fused call uses (the tcgen05 one; for
-    M <= 16 the default would be the small-batch kernel, whose summation order
-    differs)."""
-    nt = 16 if x.shape[0] <= 16 else 0
-    return ops.gemm(x, blob, K, N, G, bias=bias, ntok=nt)
+    """The plain GEMM; the fused call runs the same kernel and plan (the
+    small-batch kernel for small M, the tcgen05 kernel above), so a world of
+    one must reproduce it bit for bit."""
+    return ops.gemm(x, blob, K, N, G, bias=bias)
 
 
 def _blob(cuda, K, N, G, dt, seed):
@@ -41,7 +40,7 @@ def test_fused_equals_plain_gemm(cuda, exchange, K, N, mode):
     exchange.set_mode(mode)
     w, blob = _blob(cuda, K, N, G, dt, K + N)
     for rep in range(3):  # consecutive calls alternate the landing / flag parity
-        for M in (1, 5, 33, 64):
+        for M in (1, 5, 8, 16, 17, 33, 64):
             x = make_activations(M, K, dt, seed=M + rep).to(cuda)
             y = exchange.gemm_allreduce(x, blob, K, N, G)
             assert torch.equal(y, _plain(x, blob, K, N, G)), (K, N, M, rep, ops.gemm_plan(M, K, N, G))
