@@ -389,14 +389,15 @@ constexpr int64_t kGemvSmemAlone = 160 * 1024;
 constexpr int64_t kGemvSmemFixed = 1024 + 256;  // alignment slack + barriers
 
 // Configuration, from sweeps on B200 over the Llama-3-8B decode projections
-// (M = 1..16, every built slice / warp count / ring depth):
-//  * outputs of at least 16384 features: 8 warps, 32-feature slices (many
-//    CTAs, two or three per SM);
-//  * 8 or more rows and at least 6144 features: 8 warps, 64-feature slices
-//    (the activation tile is read once per 64 features);
-//  * more than 8 rows otherwise: 8 warps, 32-feature slices;
-//  * up to 8 rows otherwise: 16 warps per CTA (few CTAs: more warps per SM),
-//    with 16-feature slices for up to 4 rows over K <= 4096 and 32 otherwise.
+// (M = 1..16, every built slice / warp count / ring depth). What matters most
+// is that the CTAs fit on the SMs in one wave: a 16-warp CTA with 32-feature
+// slices takes one SM, an 8-warp CTA a third of one.
+//  * more than 8 rows: 8 warps, 64-feature slices from 6144 outputs (the
+//    activation tile is read once per 64 features), 32 below;
+//  * outputs of at least 16384 features: 8 warps, 64-feature slices;
+//  * at least 6144: 8 warps, 32-feature slices;
+//  * narrower outputs: 16 warps per CTA (few CTAs: more warps per SM), with
+//    32-feature slices, or 16 when that would leave fewer than 100 CTAs.
 // ring = shared-memory stages: as many as the budget allows once the CTAs are
 // spread over the SMs.
 int gemv_plan(int64_t M, int64_t K, int64_t N, int64_t G, int F_req, int W_req, int ring_req, GemvPlan* gp) {
@@ -413,19 +414,18 @@ int gemv_plan(int64_t M, int64_t K, int64_t N, int64_t G, int F_req, int W_req, 
   gp->gpb = groups_per_block((int)G);
   int W = W_req, F = F_req;
   if (W == 0 && F == 0) {
-    if (N >= 16384) {
-      W = 8, F = 32;
-    } else if (M >= 8 && M <= 16 && N >= 6144) {
+    if (M > 8) {
+      W = 8, F = (N >= 6144 && M <= 16) ? 64 : 32;
+    } else if (N >= 16384) {
       W = 8, F = 64;
-    } else if (M > 8) {
+    } else if (N >= 6144) {
       W = 8, F = 32;
     } else {
-      W = 16;
-      F = (M <= 4 && K <= 4096 && (N + 15) / 16 <= 2 * sm) ? 16 : 32;
+      W = 16, F = (N + 31) / 32 < 100 ? 16 : 32;
     }
   }
-  if (W == 0) W = (F == 16) ? 16 : (F == 64) ? 8 : (N >= 16384 || M > 8 ? 8 : 16);
-  if (F == 0) F = (W == 8) ? 32 : ((M <= 4 && K <= 4096 && (N + 15) / 16 <= 2 * sm) ? 16 : 32);
+  if (W == 0) W = (F == 16) ? 16 : (F == 64 || N >= 6144 || M > 8) ? 8 : 16;
+  if (F == 0) F = (W == 16) ? ((N + 31) / 32 < 100 ? 16 : 32) : 32;
   AWQB_REQUIRE(gemv_built(F, W), kUnsupported, "small-batch kernel with %d-feature slices and %d warps not built",
                F, W);
   const int64_t sb = gemv_stage_bytes_rt(F, W, gp->gpb, (int)M);

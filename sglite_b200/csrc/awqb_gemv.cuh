@@ -25,21 +25,24 @@
 // narrow outputs (few CTAs: more warps per SM), eight suit wide ones (more,
 // smaller CTAs per SM).
 //
-// Arithmetic: the dequantiser turns a nibble pair into the exact 16-bit values
-// OFF + q (OFF = 128 for bf16, 1024 for fp16: one lop3) and subtracts OFF + z
-// (exact), giving the integers q - z as MMA operand A; the tensor core
-// accumulates D = sum_k (q_k - z) x_k over a group in fp32 (the first MMA of a
-// group starts from zero) and the group adds s * D to the fp32 accumulator.
-// This is the reference's sum of x * (q - z) * s without its rounding of each
-// dequantised weight to 16 bits (the GEMM contract is max |y - ref| <= 1e-2
-// max |ref| against an fp32 accumulation of the reference's weights; the
-// dequantised weights themselves stay bit-exact in awqb_dequant). Measured on
-// B200: the shift + lop3 pairs run on the 64-lane integer pipe and the
-// subtract on the floating-point pipe; the kernel is bound by instruction
-// issue, so the loop keeps per-block overheads (ring bookkeeping, zero and
-// scale unpacking, accumulator set-up) to a few instructions per word and
-// runs sixteen warps per CTA (folding the scale into operand A, or spreading a
-// group over more accumulator chains, measured slower).
+// Arithmetic: the dequantiser only turns a nibble pair into the exact 16-bit
+// values OFF + q (OFF = 128 for bf16, 1024 for fp16: one lop3 per pair); the
+// tensor core accumulates D = sum_k (OFF + q_k) x_k over a group in fp32 (the
+// first MMA of a group starts from zero) and, with an all-ones operand A,
+// X = sum_k x_k; the group then adds s * (D - (OFF + z) X) to the fp32
+// accumulator. This is the reference's sum of x * (q - z) * s without its
+// rounding of each dequantised weight to 16 bits (the GEMM contract is
+// max |y - ref| <= 1e-2 max |ref| against an fp32 accumulation of the
+// reference's weights; the dequantised weights themselves stay bit-exact in
+// awqb_dequant). The cancellation in D - (OFF + z) X costs at most 11 of fp32's
+// 24 bits. Measured on B200: the kernel is bound by instruction issue (the
+// shift + lop3 pairs run on the 64-lane integer pipe), so the loop keeps
+// per-block overheads (ring bookkeeping, zero and scale unpacking, accumulator
+// set-up) to a few instructions per word, takes the zero point out of the
+// per-weight work (one all-ones MMA per two weight MMAs instead of four
+// subtractions per word), and runs sixteen warps per CTA for narrow outputs
+// (folding the scale into operand A, or more accumulator chains per group,
+// measured slower).
 //
 #pragma once
 #include <cuda.h>
@@ -108,6 +111,8 @@ struct GemvCfg {
 template <typename T> struct GemvTraits;
 template <> struct GemvTraits<__half> {
   static constexpr uint32_t kMagic = 0x64006400u;  // 1024 in both halves: OR-ing q gives 1024 + q
+  static constexpr uint32_t kOnes = 0x3C003C00u;   // 1.0 in both halves
+  static constexpr float kOff = 1024.0f;
   // (1024 + z) in both halves, exact
   __device__ __forceinline__ static uint32_t zero2(uint32_t z) { return (0x6400u | z) * 0x00010001u; }
   __device__ __forceinline__ static uint32_t sub2(uint32_t a, uint32_t b) {
@@ -120,6 +125,8 @@ template <> struct GemvTraits<__half> {
 };
 template <> struct GemvTraits<__nv_bfloat16> {
   static constexpr uint32_t kMagic = 0x43004300u;  // 128 in both halves: OR-ing q gives 128 + q
+  static constexpr uint32_t kOnes = 0x3F803F80u;   // 1.0 in both halves
+  static constexpr float kOff = 128.0f;
   __device__ __forceinline__ static uint32_t zero2(uint32_t z) { return (0x4300u | z) * 0x00010001u; }
   __device__ __forceinline__ static uint32_t sub2(uint32_t a, uint32_t b) {
     uint32_t r;
@@ -321,7 +328,7 @@ __device__ __noinline__ void gemv_exchange(const GemvParams& p, const float* red
 //   tm_z: u32 {16 words, GPB groups, KB, NT},                            box {kZWords, GPB, W, 1}
 //   tm_x: u16 {32 k, M rows, K / 32 chunks},                             box {32, M, 4 W}
 template <typename T, int F, int MT, int GPB, int W>
-__global__ void __launch_bounds__(GemvCfg<F, MT, GPB, W>::kThreads)
+__global__ void __launch_bounds__(GemvCfg<F, MT, GPB, W>::kThreads, F == 16 ? 2 : 1)
 awq_gemv_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_s,
                 const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_x,
                 const __grid_constant__ GemvParams p) {
@@ -462,19 +469,20 @@ awq_gemv_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
                   wa[rg][q + 1][1]);
 #pragma unroll
       for (int grp = 0; grp < GPB; ++grp) {
-        // (OFF + z) pairs and scales of rows g and g + 8 of every row group
-        uint32_t zr[Cfg::kRG][2];
-        float sc[Cfg::kRG][2];
+        // OFF + z and the scales of rows g and g + 8 of every row group
+        float oz[Cfg::kRG][2], sc[Cfg::kRG][2];
 #pragma unroll
         for (int rg = 0; rg < Cfg::kRG; ++rg)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const uint32_t zw = lds32(st + z_off + (uint32_t)((grp * Cfg::kZWords + rg * 2 + h) * 4));
-            zr[rg][h] = Tr::zero2((zw >> (4 * g)) & 0xFu);
+            oz[rg][h] = Tr::kOff + (float)((zw >> (4 * g)) & 0xFu);
             sc[rg][h] = Tr::to_f32((uint16_t)lds16(st + s_off + (uint32_t)((grp * F + rg * 16 + h * 8) * 2)));
           }
-        // one accumulator chain per (row group, token group) for the group
+        // one accumulator chain per (row group, token group) for the group,
+        // and the activation sums X (all-ones operand A)
         float d[Cfg::kRG][Cfg::kTG][4];
+        float xs[Cfg::kTG][4];
 #pragma unroll
         for (int qi = 0; qi < QG; ++qi) {
           const int q = grp * QG + qi;
@@ -483,35 +491,46 @@ awq_gemv_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           for (int j = 0; j < Cfg::kTG; ++j) xb[j] = lds128(st + x_off[j] + (uint32_t)q * x_qstride);
 #pragma unroll
           for (int pp = 0; pp < 2; ++pp) {
+            const bool first = qi == 0 && pp == 0;
 #pragma unroll
             for (int rg = 0; rg < Cfg::kRG; ++rg) {
               const uint32_t wg = wa[rg][q][0];
               const uint32_t wg8 = wa[rg][q][1];
-              const uint32_t a0 = Tr::sub2(nib_pair<Tr::kMagic>(wg, 2 * pp), zr[rg][0]);
-              const uint32_t a1 = Tr::sub2(nib_pair<Tr::kMagic>(wg8, 2 * pp), zr[rg][1]);
-              const uint32_t a2 = Tr::sub2(nib_pair<Tr::kMagic>(wg, 2 * pp + 1), zr[rg][0]);
-              const uint32_t a3 = Tr::sub2(nib_pair<Tr::kMagic>(wg8, 2 * pp + 1), zr[rg][1]);
+              const uint32_t a0 = nib_pair<Tr::kMagic>(wg, 2 * pp);
+              const uint32_t a1 = nib_pair<Tr::kMagic>(wg8, 2 * pp);
+              const uint32_t a2 = nib_pair<Tr::kMagic>(wg, 2 * pp + 1);
+              const uint32_t a3 = nib_pair<Tr::kMagic>(wg8, 2 * pp + 1);
 #pragma unroll
               for (int j = 0; j < Cfg::kTG; ++j) {
                 const uint32_t b0 = pp == 0 ? xb[j].x : xb[j].z;
                 const uint32_t b1 = pp == 0 ? xb[j].y : xb[j].w;
-                if (qi == 0 && pp == 0)
+                if (first)
                   mma16816_z<T>(d[rg][j], a0, a1, a2, a3, b0, b1);
                 else
                   mma16816<T>(d[rg][j], a0, a1, a2, a3, b0, b1);
               }
             }
+#pragma unroll
+            for (int j = 0; j < Cfg::kTG; ++j) {
+              const uint32_t b0 = pp == 0 ? xb[j].x : xb[j].z;
+              const uint32_t b1 = pp == 0 ? xb[j].y : xb[j].w;
+              if (first)
+                mma16816_z<T>(xs[j], Tr::kOnes, Tr::kOnes, Tr::kOnes, Tr::kOnes, b0, b1);
+              else
+                mma16816<T>(xs[j], Tr::kOnes, Tr::kOnes, Tr::kOnes, Tr::kOnes, b0, b1);
+            }
           }
         }
-        // acc += s * D for rows g and g + 8
+        // acc += s * (D - (OFF + z) * X) for rows g and g + 8 (X of tokens
+        // 2t and 2t + 1 sits in the first two elements of the ones product)
 #pragma unroll
         for (int rg = 0; rg < Cfg::kRG; ++rg)
 #pragma unroll
           for (int j = 0; j < Cfg::kTG; ++j) {
-            acc[rg][j][0] = fmaf(sc[rg][0], d[rg][j][0], acc[rg][j][0]);
-            acc[rg][j][1] = fmaf(sc[rg][0], d[rg][j][1], acc[rg][j][1]);
-            acc[rg][j][2] = fmaf(sc[rg][1], d[rg][j][2], acc[rg][j][2]);
-            acc[rg][j][3] = fmaf(sc[rg][1], d[rg][j][3], acc[rg][j][3]);
+            acc[rg][j][0] = fmaf(sc[rg][0], fmaf(-oz[rg][0], xs[j][0], d[rg][j][0]), acc[rg][j][0]);
+            acc[rg][j][1] = fmaf(sc[rg][0], fmaf(-oz[rg][0], xs[j][1], d[rg][j][1]), acc[rg][j][1]);
+            acc[rg][j][2] = fmaf(sc[rg][1], fmaf(-oz[rg][1], xs[j][0], d[rg][j][2]), acc[rg][j][2]);
+            acc[rg][j][3] = fmaf(sc[rg][1], fmaf(-oz[rg][1], xs[j][1], d[rg][j][3]), acc[rg][j][3]);
           }
       }
     }
