@@ -342,15 +342,16 @@ struct TpExchange {
 constexpr int kGemvMaxM = 32;
 
 // Whether awqb_gemm takes the small-batch kernel (measured against the
-// tcgen05 kernel on B200 over the Llama-3-8B decode projections): up to 8 rows
-// always; up to 16 rows unless the output is wide (N >= 16384: gate_up at
-// M = 12 / 16, 21.1 vs 25.6 us) or K long (K > 8192: down at M = 16, 14.2 vs
-// 14.4 us); up to 32 rows for problems of at most 16 Mi weights (O 4096 x 4096
-// at M = 32: 8.3 vs 8.7 us). Above, the tcgen05 kernel's larger MMAs win.
+// tcgen05 kernel on B200 over the Llama-3-8B decode projections, whole and
+// sharded 8 ways): up to 8 rows always; up to 16 rows unless the output is
+// wide (N >= 16384: gate_up at M = 16, 21.3 vs 26.5 us; down at M = 16 is
+// 13.2 vs 14.2 us); up to 32 rows for problems of at most 16 Mi weights
+// (O 4096 x 4096 at M = 32: 8.0 vs 8.7 us). Above, the tcgen05 kernel's
+// larger MMAs win.
 bool gemv_takes(int64_t M, int64_t K, int64_t N) {
   if (M < 1 || M > kGemvMaxM) return false;
   if (M <= 8) return true;
-  if (M <= 16) return N < 16384 && K <= 8192;
+  if (M <= 16) return N < 16384;
   return K * N <= (16ll << 20);
 }
 
@@ -415,7 +416,10 @@ int gemv_plan(int64_t M, int64_t K, int64_t N, int64_t G, int F_req, int W_req, 
   int W = W_req, F = F_req;
   if (W == 0 && F == 0) {
     if (M > 8) {
-      W = 8, F = (N >= 6144 && M <= 16) ? 64 : 32;
+      if (M <= 16 && N < 2048)
+        W = 16, F = 16;  // few slices: more warps per CTA
+      else
+        W = 8, F = (N >= 6144 && M <= 16) ? 64 : 32;
     } else if (N >= 16384) {
       W = 8, F = 64;
     } else if (N >= 6144) {
