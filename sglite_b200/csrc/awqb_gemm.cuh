@@ -326,21 +326,30 @@ __device__ __noinline__ void tp_cluster_finish(const GemmParams& p, int n0, int 
       const uint16_t b = (uint16_t)(w & 0xffffu);
       out = *reinterpret_cast<const T*>(&b);
     } else {
-      float v = 0.f;
-      for (int r = 0; r < p.tp_world; ++r) {
-        const uint2* wp = land + ((int64_t)r * p.tp_rows + m) * p.N + n;
-        uint2 w = ld_tagged_sys(wp);
-        while (w.y != tag) {
+      // every rank's word of this value in flight at once, then the laggards
+      const uint2* wp = land + (int64_t)m * p.N + n;
+      const int64_t rstride = (int64_t)p.tp_rows * p.N;
+      uint2 w[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < p.tp_world) w[r] = ld_tagged_sys(wp + r * rstride);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r >= p.tp_world) break;
+        while (w[r].y != tag) {
           if (t0 == 0) {
             t0 = globaltimer_ns();
           } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
             atomicOr(p.err, 8u);
             return;
           }
-          w = ld_tagged_sys(wp);
+          w[r] = ld_tagged_sys(wp + r * rstride);
         }
-        v += __uint_as_float(w.x);
       }
+      float v = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < p.tp_world) v += __uint_as_float(w[r].x);  // rank order
       if (p.bias != nullptr) v += (float)reinterpret_cast<const T*>(p.bias)[n];
       out = (T)v;
       if (p.tp_rsag) {
@@ -1224,11 +1233,12 @@ awq_gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constan
   }
   if (p.tp_world > 0 && threadIdx.x == 0) {
     // The last CTA to finish advances this rank's call counter (the parity of
-    // the next fused call); the next kernel reads it after the grid boundary.
-    __threadfence();
+    // the next fused call). Every CTA read the counter before it counted
+    // itself done, and the next kernel reads it after the grid boundary, so
+    // no fence is needed (one after the stores to peer memory would wait for
+    // their acknowledgements over NVLink).
     if (atomicAdd(p.tp_epoch + 1, 1) == (int)gridDim.x - 1) {
       p.tp_epoch[1] = 0;
-      __threadfence();
       atomicAdd(p.tp_epoch, 1);
     }
   }

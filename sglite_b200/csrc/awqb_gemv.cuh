@@ -284,23 +284,31 @@ __device__ __noinline__ void gemv_exchange(const GemvParams& p, const float* red
       if (!ok) break;
       out = (uint16_t)(w & 0xffffu);
     } else {
-      float v = 0.f;
-      const uint2* land = p.tp_land[rank] + (int64_t)par * p.tp_half;
-      for (int r = 0; ok && r < world; ++r) {
-        const uint2* wp = land + ((int64_t)r * p.tp_rows + n) * p.N + col;
-        uint2 w = ld_tagged_sys(wp);
-        while (w.y != tag) {
+      // every rank's word of this value in flight at once, then the laggards
+      const uint2* land = p.tp_land[rank] + (int64_t)par * p.tp_half + (int64_t)n * p.N + col;
+      const int64_t rstride = (int64_t)p.tp_rows * p.N;
+      uint2 w[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < world) w[r] = ld_tagged_sys(land + r * rstride);
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r >= world) break;
+        while (w[r].y != tag) {
           if (t0 == 0) {
             t0 = globaltimer_ns();
           } else if (globaltimer_ns() - t0 > AWQB_WAIT_TIMEOUT_NS) {
             ok = false;
             break;
           }
-          w = ld_tagged_sys(wp);
+          w[r] = ld_tagged_sys(land + r * rstride);
         }
-        v += __uint_as_float(w.x);
       }
       if (!ok) break;
+      float v = 0.f;
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < world) v += __uint_as_float(w[r].x);  // rank order
       if (p.bias != nullptr) v += Tr::to_f32(reinterpret_cast<const uint16_t*>(p.bias)[col]);
       out = Tr::from_f32(v);
       if (rsag) {
@@ -316,11 +324,12 @@ __device__ __noinline__ void gemv_exchange(const GemvParams& p, const float* red
   named_bar_sync(1, nthreads);
   if (tid == 0) {
     // The last CTA to finish advances this rank's call counter (the parity of
-    // the next fused call); the next kernel reads it after the grid boundary.
-    __threadfence();
+    // the next fused call). Every CTA read the counter before it counted
+    // itself done, and the next kernel reads it after the grid boundary, so
+    // no fence is needed (one after the stores to peer memory would wait for
+    // their acknowledgements over NVLink).
     if (atomicAdd(p.tp_epoch + 1, 1) == (int)gridDim.x - 1) {
       p.tp_epoch[1] = 0;
-      __threadfence();
       atomicAdd(p.tp_epoch, 1);
     }
   }
