@@ -164,3 +164,72 @@ def test_awq_moe_layer_from_a_checkpoint_against_the_oracle(cuda):
         parts.append(lr.forward(x.to(cuda).clone(), logits.to(cuda)).float())
     assert rel_err(parts[0] + parts[1], ref) <= 1e-2
     assert ops.device_error() == 0
+
+
+def _vllm_ops():
+    try:
+        import vllm._custom_ops as vops  # noqa: F401
+    except Exception as e:  # pragma: no cover - depends on the image
+        pytest.skip(f"vllm custom ops unavailable: {e}")
+    return vops
+
+
+@pytest.mark.parametrize("M,E,k", [(1, 128, 8), (37, 128, 8), (300, 16, 4), (4096, 128, 8)])
+@pytest.mark.parametrize("renorm", [True, False])
+def test_topk_softmax_matches_vllm(cuda, M, E, k, renorm):
+    """The reference's fused_topk (fused.py:11-31) calls sgl-kernel's
+    topk_softmax, which is absent here; vllm's topk_softmax (installed on the
+    GPU image) implements the same routing kernel. With the reference's Python
+    renormalisation after it, ids must match exactly and weights to 1e-6."""
+    vops = _vllm_ops()
+    lg = make_router_logits(M, E, seed=M * 3 + E).to(cuda)
+    w_v = torch.empty((M, k), dtype=torch.float32, device=cuda)
+    i_v = torch.empty((M, k), dtype=torch.int32, device=cuda)
+    tei = torch.empty((M, k), dtype=torch.int32, device=cuda)
+    try:
+        vops.topk_softmax(w_v, i_v, tei, lg.float(), renorm)
+        torch.cuda.synchronize()
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"vllm topk_softmax failed to run here: {e}")
+    if renorm:
+        w_v = w_v / (w_v.sum(dim=-1, keepdim=True) + 1e-8)
+    w, ids = ops.moe_topk_softmax(lg, k, renorm)
+    assert torch.equal(ids.cpu(), i_v.cpu())
+    assert torch.allclose(w.cpu(), w_v.cpu(), rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("M,E,k,bm", [(1, 128, 8, 16), (256, 128, 8, 32), (4096, 128, 8, 128), (999, 16, 4, 64)])
+def test_align_matches_vllm(cuda, M, E, k, bm):
+    """moe_align_block_size (fused.py:34-61; sgl-kernel, absent) against
+    vllm's kernel of the same name: identical padded length and block experts,
+    and every expert's padded region (its consecutive blocks) holds the same
+    pair indices (the order inside a region is the kernel's own: ours is
+    stable, which the oracle tests check; vllm's is not)."""
+    vops = _vllm_ops()
+    ids = torch.stack([torch.randperm(E, generator=torch.Generator().manual_seed(i))[:k]
+                       for i in range(M)]).to(torch.int32).to(cuda)
+    numel = ids.numel()
+    cap = numel + E * (bm - 1)
+    s_v = torch.full((cap,), numel, dtype=torch.int32, device=cuda)
+    e_v = torch.zeros(((cap + bm - 1) // bm,), dtype=torch.int32, device=cuda)
+    n_v = torch.zeros((1,), dtype=torch.int32, device=cuda)
+    try:
+        vops.moe_align_block_size(ids, E, bm, s_v, e_v, n_v)
+        torch.cuda.synchronize()
+    except Exception as e:  # pragma: no cover
+        pytest.skip(f"vllm moe_align_block_size failed to run here: {e}")
+    sorted_ids, block_expert, npp = ops.moe_align(ids, 0, E, bm)
+    n = int(npp.item())
+    assert n == int(n_v.item())
+    assert torch.equal(block_expert[: n // bm].cpu(), e_v[: n // bm].cpu())
+    ours, theirs = sorted_ids[:n].cpu(), s_v[:n].cpu()
+    be = block_expert[: n // bm].cpu().tolist()
+    b0 = 0
+    while b0 < len(be):  # one expert's consecutive blocks at a time
+        b1 = b0
+        while b1 < len(be) and be[b1] == be[b0]:
+            b1 += 1
+        a, c = ours[b0 * bm:b1 * bm], theirs[b0 * bm:b1 * bm]
+        assert torch.equal(torch.sort(a).values, torch.sort(c).values), be[b0]
+        b0 = b1
+    assert ops.device_error() == 0
